@@ -1,0 +1,1113 @@
+// Fused 2D-RoPE + variable-length attention forward for B200 (sm_100a).
+//
+// Operation (reference: sdan/fused-rope-attn fused_attn.py:246-423, the Triton
+// `fused_attn_kernel`, and its wrapper fused_attn.py:139-232):
+//   for each cu_seqlens segment s and head h,
+//     O = softmax(R(Q) R(K)^T / sqrt(D)) V
+//   with R = rotate-half RoPE, computed in fp32 and rounded to the input type
+//   before the product (fused_attn.py:340-345, 385-390), fp32 online softmax in
+//   base 2 (fused_attn.py:353-405), fp32 accumulation and a final 1/l
+//   (fused_attn.py:417-423).
+//
+// Design (B200-native, not a translation of the Triton program grid):
+//   * An on-device scheduler kernel (`build_worklist`) turns cu_seqlens into a
+//     list of 128-row work items in the workspace, so no host sync is needed:
+//       - "long" items: 128-row q tiles of segments longer than 128 tokens, each
+//         attending to its whole segment;
+//       - "packed" items: the rows of all short (<= 128 token) segments that
+//         start inside one 128-row chunk of the packed sequence, batched into
+//         one M=128 tile with a per-row segment mask. Two 64-token windows
+//         therefore share one tensor-core tile instead of two half-empty ones.
+//   * One persistent CTA per SM walks (item, head) units. Warp roles:
+//       warp 0      TMA producer (Q, K, V tiles; 32-B swizzled, 16-column blocks)
+//       warp 1      tcgen05 MMA issuer + TMEM owner
+//       warps 2-3   RoPE: rotate the raw Q/K tiles in shared memory in place
+//       warps 4-7   softmax + O correction + epilogue, one thread per q row
+//   * S = Q K^T (M=128, N=128, K=D) and O += P V (M=128, N=D, K=128) run on the
+//     5th-gen tensor cores with fp32 accumulators in TMEM (S double-buffered).
+//   * Every mbarrier wait is bounded; on timeout the kernel records a status
+//     code and returns instead of hanging the GPU.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+#include <type_traits>
+
+#include "../../include/frattn.h"
+#include "frattn_ptx.cuh"
+
+namespace frattn {
+
+constexpr int kTileM = 128;   // q rows per tile (TMEM lanes)
+constexpr int kTileN = 128;   // kv rows per tile
+constexpr int kThreads = 256; // 8 warps
+constexpr int kRopeThreads = 64;
+constexpr int kSoftmaxThreads = 128;
+constexpr int kBlkBytes = kTileM * 32;  // one 16-column (32 B) block of a 128-row tile
+
+enum ItemKind : int { kItemLong = 0, kItemPacked = 1 };
+
+struct __align__(16) WorkItem {
+  int q0, q1;      // q rows [q0, q1) stored by this item
+  int kv0, kv1;    // kv rows [kv0, kv1) attended to
+  int seg_lo, seg_hi;  // segment index range covered (packed items)
+  int kind, pad;
+};
+
+constexpr int kHeaderBytes = 128;
+__host__ __device__ inline size_t max_items(int T) {
+  const size_t chunks = (static_cast<size_t>(T) + kTileM - 1) / kTileM;
+  return 3 * chunks + 2;
+}
+
+// Rotary angle source: materialised tables (reference API) or (h, w) ids.
+enum RopeMode : int { kRopeTable = 0, kRopePos = 1 };
+
+struct Params {
+  CUtensorMap tmq, tmk, tmv;
+  const void* cos;          // [T, D/2] (table mode)
+  const void* sin;
+  const int32_t* pos_hw;    // [T, 2] (pos mode)
+  const float* pos_tab;     // [P, D/4] cos then [P, D/4] sin (pos mode)
+  int pos_rows;
+  const int32_t* cu;
+  int nseg;
+  void* out;
+  const WorkItem* items;
+  const int* header;
+  int T, H;
+  int32_t* status;
+  unsigned long long wait_limit_ns;
+};
+
+template <int D>
+struct Cfg {
+  static_assert(D % 16 == 0 && D >= 32 && D <= 128, "D must be a multiple of 16 in [32,128]");
+  static constexpr int KB = D / 16;                  // column blocks per row
+  static constexpr int TILE_BYTES = kTileM * D * 2;  // one 128 x D bf16 tile
+  static constexpr int STAGES = D <= 96 ? 3 : 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + 2 * TILE_BYTES;
+  static constexpr int OFF_V = OFF_K + STAGES * TILE_BYTES;
+  static constexpr int OFF_P = OFF_V + STAGES * TILE_BYTES;
+  static constexpr int P_BYTES = kTileM * kTileN * 2;
+  static constexpr int OFF_BAR = OFF_P + P_BYTES;
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int SMEM_BYTES = OFF_BAR + BAR_BYTES + 1024;  // +1024 alignment slack
+  // TMEM columns: S0 [0,128), S1 [128,256), O [256, 256 + D)
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t TMEM_S0 = 0;
+  static constexpr uint32_t TMEM_O = 256;
+};
+
+// barrier slots (each 8 bytes)
+template <int STAGES>
+struct Bars {
+  static constexpr int Q_FULL = 0;                 // [2]
+  static constexpr int Q_READY = 2;                // [2]
+  static constexpr int Q_EMPTY = 4;                // [2]
+  static constexpr int K_FULL = 6;                 // [STAGES]
+  static constexpr int K_READY = K_FULL + STAGES;  // [STAGES]
+  static constexpr int K_EMPTY = K_READY + STAGES;
+  static constexpr int V_FULL = K_EMPTY + STAGES;
+  static constexpr int V_EMPTY = V_FULL + STAGES;
+  static constexpr int S_FULL = V_EMPTY + STAGES;  // [2]
+  static constexpr int S_FREE = S_FULL + 2;        // [2]
+  static constexpr int P_FULL = S_FREE + 2;
+  static constexpr int P_EMPTY = P_FULL + 1;
+  static constexpr int DONE = P_EMPTY + 1;
+  static constexpr int COUNT = DONE + 1;
+};
+
+// ------------------------------------------------------------------ helpers
+struct Ctl {
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity, const Params& p,
+                                             volatile int* abort_flag, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t n = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if ((++n & 15u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > p.wait_limit_ns) {
+        *abort_flag = 1;
+        if (p.status) atomicCAS(reinterpret_cast<int*>(p.status), 0, code);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// Warp-uniform bounded wait (every lane polls; the warp agrees on the result so
+// that the following .sync.aligned tcgen05 instructions never diverge).
+__device__ __forceinline__ bool bounded_wait_warp(uint32_t bar, uint32_t parity, const Params& p,
+                                                  volatile int* abort_flag, int code) {
+  const bool ok = bounded_wait(bar, parity, p, abort_flag, code);
+  return __all_sync(0xffffffffu, ok);
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T x);
+template <>
+__device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+
+// Load 8 consecutive values of a cos/sin table row as fp32.
+template <typename TC>
+__device__ __forceinline__ void load8(const TC* src, float (&v)[8]);
+template <>
+__device__ __forceinline__ void load8<float>(const float* src, float (&v)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* src, float (&v)[8]) {
+  const uint4 a = __ldg(reinterpret_cast<const uint4*>(src));
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&a);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void load8<__half>(const __half* src, float (&v)[8]) {
+  const uint4 a = __ldg(reinterpret_cast<const uint4*>(src));
+  const __half2* h = reinterpret_cast<const __half2*>(&a);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+template <typename TI>
+__device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]);
+template <>
+__device__ __forceinline__ void unpack8<__nv_bfloat16>(const uint4& u, float (&v)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void unpack8<__half>(const uint4& u, float (&v)[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+template <typename TI>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Address of the 16-byte chunk `c` (8 elements) of row r inside a 128-row tile
+// stored as [column block][row][32 B] with the TMA/UMMA 32-byte swizzle
+// (16-byte halves of rows 4..7 of every 8-row group are swapped).
+__device__ __forceinline__ uint32_t chunk_off(int r, int c) {
+  return static_cast<uint32_t>((c >> 1) * kBlkBytes + r * 32 +
+                               ((((c & 1) ^ (r >> 2)) & 1) << 4));
+}
+
+// Rotary cos/sin for 8 consecutive rotary indices [i0, i0+8) of token `row`.
+template <int D, int MODE, typename TC>
+__device__ __forceinline__ void rope_coeffs(const Params& p, int row, int i0, float (&cs)[8],
+                                            float (&sn)[8]) {
+  if constexpr (MODE == kRopeTable) {
+    const TC* c = static_cast<const TC*>(p.cos) + static_cast<size_t>(row) * (D / 2) + i0;
+    const TC* s = static_cast<const TC*>(p.sin) + static_cast<size_t>(row) * (D / 2) + i0;
+    load8<TC>(c, cs);
+    load8<TC>(s, sn);
+  } else {
+    constexpr int Q4 = D / 4;
+    const int2 hw = __ldg(reinterpret_cast<const int2*>(p.pos_hw) + row);
+    const float* ct = p.pos_tab;
+    const float* st = p.pos_tab + static_cast<size_t>(p.pos_rows) * Q4;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int i = i0 + e;
+      const int pos = i < Q4 ? hw.x : hw.y;
+      const int j = i < Q4 ? i : i - Q4;
+      const size_t idx = static_cast<size_t>(pos) * Q4 + j;
+      cs[e] = __ldg(ct + idx);
+      sn[e] = __ldg(st + idx);
+    }
+  }
+}
+
+// Rotate a raw 128 x D tile in shared memory in place (rotate-half RoPE,
+// fp32 math, one rounding to the element type, fused_attn.py:340-345).
+template <int D, int MODE, typename TI, typename TC>
+__device__ __forceinline__ void rope_tile(uint8_t* tile, int row0, const Params& p, int tid) {
+  constexpr int NP = D / 16;  // pairs of 8-element chunks: chunk c <-> chunk c + NP
+  for (int u = tid; u < kTileM * NP; u += kRopeThreads) {
+    const int r = u & (kTileM - 1);
+    const int c = u >> 7;
+    const int row = row0 + r;
+    if (row >= p.T) continue;
+    uint4* pa = reinterpret_cast<uint4*>(tile + chunk_off(r, c));
+    uint4* pb = reinterpret_cast<uint4*>(tile + chunk_off(r, c + NP));
+    float x0[8], x1[8], cs[8], sn[8];
+    unpack8<TI>(*pa, x0);
+    unpack8<TI>(*pb, x1);
+    rope_coeffs<D, MODE, TC>(p, row, c * 8, cs, sn);
+    uint4 oa, ob;
+    uint32_t* wa = reinterpret_cast<uint32_t*>(&oa);
+    uint32_t* wb = reinterpret_cast<uint32_t*>(&ob);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const float a0 = x0[e] * cs[e] - x1[e] * sn[e];
+      const float a1 = x0[e + 1] * cs[e + 1] - x1[e + 1] * sn[e + 1];
+      const float b0 = x0[e] * sn[e] + x1[e] * cs[e];
+      const float b1 = x0[e + 1] * sn[e + 1] + x1[e + 1] * cs[e + 1];
+      wa[e / 2] = pack2<TI>(a0, a1);
+      wb[e / 2] = pack2<TI>(b0, b1);
+    }
+    *pa = oa;
+    *pb = ob;
+  }
+}
+
+__device__ __forceinline__ int upper_bound_cu(const int32_t* cu, int lo, int hi, int x) {
+  // first index i in [lo, hi) with cu[i] > x (hi if none)
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (__ldg(cu + mid) > x) hi = mid; else lo = mid + 1;
+  }
+  return lo;
+}
+
+// ------------------------------------------------------------------ kernel
+template <int D, int MODE, typename TI, typename TC>
+__global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __grid_constant__ Params p) {
+  using C = Cfg<D>;
+  using B = Bars<C::STAGES>;
+  constexpr int ST = C::STAGES;
+  constexpr bool kBF16 = std::is_same<TI, __nv_bfloat16>::value;
+  constexpr uint32_t IDESC_S = make_idesc_f16(kBF16, kTileM, kTileN, false);
+  constexpr uint32_t IDESC_O = make_idesc_f16(kBF16, kTileM, D, true);
+  constexpr uint32_t SW32 = 6;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + C::OFF_BAR;
+  auto bar = [&](int i) -> uint32_t { return bar0 + 8u * static_cast<uint32_t>(i); };
+  Ctl* ctl = reinterpret_cast<Ctl*>(smem + C::OFF_BAR + 8 * B::COUNT);
+  volatile int* abort_flag = &ctl->abort;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(B::Q_FULL + i), 1);
+      mbar_init(bar(B::Q_READY + i), kRopeThreads);
+      mbar_init(bar(B::Q_EMPTY + i), 1);
+      mbar_init(bar(B::S_FULL + i), 1);
+      mbar_init(bar(B::S_FREE + i), kSoftmaxThreads);
+    }
+    for (int i = 0; i < ST; ++i) {
+      mbar_init(bar(B::K_FULL + i), 1);
+      mbar_init(bar(B::K_READY + i), kRopeThreads);
+      mbar_init(bar(B::K_EMPTY + i), 1);
+      mbar_init(bar(B::V_FULL + i), 1);
+      mbar_init(bar(B::V_EMPTY + i), 1);
+    }
+    mbar_init(bar(B::P_FULL), kSoftmaxThreads);
+    mbar_init(bar(B::P_EMPTY), 1);
+    mbar_init(bar(B::DONE), 1);
+    ctl->abort = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&p.tmq);
+    tma_prefetch_desc(&p.tmk);
+    tma_prefetch_desc(&p.tmv);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+
+  const int n_items = __ldg(p.header);
+  const int n_units = n_items * p.H;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t q_it = 0, k_it = 0, v_it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+        const WorkItem it = p.items[u / p.H];
+        const int h = u % p.H;
+        const int nkv = (it.kv1 - it.kv0 + kTileN - 1) / kTileN;
+        {
+          const int qs = q_it & 1;
+          ok = bounded_wait(bar(B::Q_EMPTY + qs), ((q_it >> 1) & 1) ^ 1, p, abort_flag,
+                            FRATTN_STATUS_WAIT_TIMEOUT | 0x00);
+          if (!ok) break;
+          mbar_arrive_expect_tx(bar(B::Q_FULL + qs), C::TILE_BYTES);
+          const uint32_t dst = sbase + C::OFF_Q + qs * C::TILE_BYTES;
+#pragma unroll
+          for (int b = 0; b < C::KB; ++b)
+            tma_load_3d(dst + b * kBlkBytes, &p.tmq, bar(B::Q_FULL + qs), 16 * b, h, it.q0);
+          ++q_it;
+        }
+        for (int j = 0; j < nkv && ok; ++j) {
+          const int row = it.kv0 + j * kTileN;
+          const int ks = k_it % ST;
+          ok = bounded_wait(bar(B::K_EMPTY + ks), ((k_it / ST) & 1) ^ 1, p, abort_flag,
+                            FRATTN_STATUS_WAIT_TIMEOUT | 0x01);
+          if (!ok) break;
+          mbar_arrive_expect_tx(bar(B::K_FULL + ks), C::TILE_BYTES);
+          const uint32_t kdst = sbase + C::OFF_K + ks * C::TILE_BYTES;
+#pragma unroll
+          for (int b = 0; b < C::KB; ++b)
+            tma_load_3d(kdst + b * kBlkBytes, &p.tmk, bar(B::K_FULL + ks), 16 * b, h, row);
+          ++k_it;
+          const int vs = v_it % ST;
+          ok = bounded_wait(bar(B::V_EMPTY + vs), ((v_it / ST) & 1) ^ 1, p, abort_flag,
+                            FRATTN_STATUS_WAIT_TIMEOUT | 0x02);
+          if (!ok) break;
+          mbar_arrive_expect_tx(bar(B::V_FULL + vs), C::TILE_BYTES);
+          const uint32_t vdst = sbase + C::OFF_V + vs * C::TILE_BYTES;
+#pragma unroll
+          for (int b = 0; b < C::KB; ++b)
+            tma_load_3d(vdst + b * kBlkBytes, &p.tmv, bar(B::V_FULL + vs), 16 * b, h, row);
+          ++v_it;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t q_it = 0, k_it = 0, v_it = 0, s_it = 0, p_it = 0;
+      bool ok = true;
+      const uint32_t pbase = sbase + C::OFF_P;
+      auto issue_s = [&](uint32_t qaddr) -> bool {
+        const int ks = k_it % ST;
+        const int sb = s_it & 1;
+        if (!bounded_wait(bar(B::S_FREE + sb), ((s_it >> 1) & 1) ^ 1, p, abort_flag,
+                          FRATTN_STATUS_WAIT_TIMEOUT | 0x10))
+          return false;
+        if (!bounded_wait(bar(B::K_READY + ks), (k_it / ST) & 1, p, abort_flag,
+                          FRATTN_STATUS_WAIT_TIMEOUT | 0x11))
+          return false;
+        tc_fence_after();
+        const uint32_t kaddr = sbase + C::OFF_K + ks * C::TILE_BYTES;
+        const uint32_t d = tmem + C::TMEM_S0 + sb * kTileN;
+#pragma unroll
+        for (int kb = 0; kb < C::KB; ++kb) {
+          const uint64_t ad = make_sdesc(qaddr + kb * kBlkBytes, 16, 256, SW32);
+          const uint64_t bd = make_sdesc(kaddr + kb * kBlkBytes, 16, 256, SW32);
+          umma_ss(d, ad, bd, IDESC_S, kb > 0 ? 1u : 0u);
+        }
+        umma_commit(bar(B::K_EMPTY + ks));
+        umma_commit(bar(B::S_FULL + sb));
+        ++k_it;
+        ++s_it;
+        return true;
+      };
+      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+        const WorkItem it = p.items[u / p.H];
+        const int nkv = (it.kv1 - it.kv0 + kTileN - 1) / kTileN;
+        const int qs = q_it & 1;
+        ok = bounded_wait(bar(B::Q_READY + qs), (q_it >> 1) & 1, p, abort_flag,
+                          FRATTN_STATUS_WAIT_TIMEOUT | 0x12);
+        if (!ok) break;
+        const uint32_t qaddr = sbase + C::OFF_Q + qs * C::TILE_BYTES;
+        ok = issue_s(qaddr);
+        for (int j = 0; j < nkv && ok; ++j) {
+          if (j + 1 < nkv) {
+            ok = issue_s(qaddr);
+            if (!ok) break;
+          }
+          if (j + 1 == nkv) umma_commit(bar(B::Q_EMPTY + qs));  // all S MMAs of this Q issued
+          const int vs = v_it % ST;
+          ok = bounded_wait(bar(B::P_FULL), p_it & 1, p, abort_flag,
+                            FRATTN_STATUS_WAIT_TIMEOUT | 0x13);
+          if (!ok) break;
+          ok = bounded_wait(bar(B::V_FULL + vs), (v_it / ST) & 1, p, abort_flag,
+                            FRATTN_STATUS_WAIT_TIMEOUT | 0x14);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t vaddr = sbase + C::OFF_V + vs * C::TILE_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < kTileN / 16; ++kk) {
+            const uint64_t ad = make_sdesc(pbase + kk * kBlkBytes, 16, 256, SW32);
+            const uint64_t bd = make_sdesc(vaddr + kk * 512, kBlkBytes, 256, SW32);
+            umma_ss(tmem + C::TMEM_O, ad, bd, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(bar(B::V_EMPTY + vs));
+          umma_commit(bar(B::P_EMPTY));
+          ++v_it;
+          ++p_it;
+        }
+        ++q_it;
+      }
+      // Drain: wait until every issued MMA has completed before TMEM is freed.
+      umma_commit(bar(B::DONE));
+      bounded_wait(bar(B::DONE), 0, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x15);
+    }
+    __syncwarp();
+  } else if (warp < 4) {
+    // ------------------------------------------------------------ RoPE warps
+    const int tid = threadIdx.x - 64;
+    uint32_t q_it = 0, k_it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+      const WorkItem it = p.items[u / p.H];
+      const int nkv = (it.kv1 - it.kv0 + kTileN - 1) / kTileN;
+      const int qs = q_it & 1;
+      ok = bounded_wait(bar(B::Q_FULL + qs), (q_it >> 1) & 1, p, abort_flag,
+                        FRATTN_STATUS_WAIT_TIMEOUT | 0x20);
+      if (!ok) break;
+      rope_tile<D, MODE, TI, TC>(smem + C::OFF_Q + qs * C::TILE_BYTES, it.q0, p, tid);
+      fence_proxy_async_smem();
+      mbar_arrive(bar(B::Q_READY + qs));
+      ++q_it;
+      for (int j = 0; j < nkv; ++j) {
+        const int ks = k_it % ST;
+        ok = bounded_wait(bar(B::K_FULL + ks), (k_it / ST) & 1, p, abort_flag,
+                          FRATTN_STATUS_WAIT_TIMEOUT | 0x21);
+        if (!ok) break;
+        rope_tile<D, MODE, TI, TC>(smem + C::OFF_K + ks * C::TILE_BYTES, it.kv0 + j * kTileN, p, tid);
+        fence_proxy_async_smem();
+        mbar_arrive(bar(B::K_READY + ks));
+        ++k_it;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax WG
+    const int t = threadIdx.x - 128;  // q row within the tile == TMEM lane
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const float sl2 = 1.4426950408889634f * rsqrtf(static_cast<float>(D));
+    uint32_t s_it = 0, p_it = 0;
+    bool ok = true;
+    uint8_t* pbuf = smem + C::OFF_P;
+    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+      const WorkItem it = p.items[u / p.H];
+      const int h = u % p.H;
+      const int nkv = (it.kv1 - it.kv0 + kTileN - 1) / kTileN;
+      const int row = it.q0 + t;
+      const bool row_ok = row < it.q1;
+      int lo = 0, hi = 0;
+      if (row_ok) {
+        if (it.kind == kItemLong) {
+          lo = it.kv0;
+          hi = it.kv1;
+        } else {
+          const int s = upper_bound_cu(p.cu, it.seg_lo, it.seg_hi + 2, row) - 1;
+          lo = __ldg(p.cu + s);
+          hi = __ldg(p.cu + s + 1);
+        }
+      }
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < nkv; ++j) {
+        const int sb = s_it & 1;
+        ok = bounded_wait_warp(bar(B::S_FULL + sb), (s_it >> 1) & 1, p, abort_flag,
+                               FRATTN_STATUS_WAIT_TIMEOUT | 0x30);
+        if (!ok) break;
+        tc_fence_after();
+        float s[kTileN];
+#pragma unroll
+        for (int c = 0; c < kTileN / 16; ++c) {
+          uint32_t r[16];
+          tmem_ld16(lane_addr + C::TMEM_S0 + sb * kTileN + c * 16, r);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) s[c * 16 + e] = __uint_as_float(r[e]);
+        }
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(bar(B::S_FREE + sb));
+        ++s_it;
+
+        const int c0 = it.kv0 + j * kTileN;
+        const int lo_r = lo - c0, hi_r = hi - c0;
+        if (lo_r > 0 || hi_r < kTileN) {
+#pragma unroll
+          for (int i = 0; i < kTileN; ++i)
+            if (i < lo_r || i >= hi_r) s[i] = -INFINITY;
+        }
+        float mx = m;
+#pragma unroll
+        for (int i = 0; i < kTileN; ++i) mx = fmaxf(mx, s[i]);
+        const float m_use = (mx == -INFINITY) ? 0.f : mx;
+        const float alpha = ex2((m - m_use) * sl2);  // m == -inf -> 0
+        const float mb = m_use * sl2;
+        float sum = 0.f;
+#pragma unroll
+        for (int i = 0; i < kTileN; ++i) {
+          s[i] = ex2(fmaf(s[i], sl2, -mb));
+          sum += s[i];
+        }
+        l = l * alpha + sum;
+        m = mx;
+
+        // P buffer / O accumulator are free once PV of the previous tile is done.
+        if (j > 0) {
+          ok = bounded_wait_warp(bar(B::P_EMPTY), (p_it - 1) & 1, p, abort_flag,
+                                 FRATTN_STATUS_WAIT_TIMEOUT | 0x31);
+          if (!ok) break;
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+            for (int c = 0; c < (D + 15) / 16; ++c) {
+              uint32_t r[16];
+              tmem_ld16(lane_addr + C::TMEM_O + c * 16, r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+              tmem_st16(lane_addr + C::TMEM_O + c * 16, r);
+            }
+            tmem_st_wait();
+          }
+        }
+        // Write P (bf16/fp16) as the K-major A operand: [kv block][row][32 B].
+        const uint32_t sw = (t >> 2) & 1;
+#pragma unroll
+        for (int kk = 0; kk < kTileN / 16; ++kk) {
+          uint4 h0, h1;
+          h0.x = pack2<TI>(s[kk * 16 + 0], s[kk * 16 + 1]);
+          h0.y = pack2<TI>(s[kk * 16 + 2], s[kk * 16 + 3]);
+          h0.z = pack2<TI>(s[kk * 16 + 4], s[kk * 16 + 5]);
+          h0.w = pack2<TI>(s[kk * 16 + 6], s[kk * 16 + 7]);
+          h1.x = pack2<TI>(s[kk * 16 + 8], s[kk * 16 + 9]);
+          h1.y = pack2<TI>(s[kk * 16 + 10], s[kk * 16 + 11]);
+          h1.z = pack2<TI>(s[kk * 16 + 12], s[kk * 16 + 13]);
+          h1.w = pack2<TI>(s[kk * 16 + 14], s[kk * 16 + 15]);
+          uint8_t* rowp = pbuf + kk * kBlkBytes + t * 32;
+          *reinterpret_cast<uint4*>(rowp + (sw << 4)) = h0;
+          *reinterpret_cast<uint4*>(rowp + ((sw ^ 1) << 4)) = h1;
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(bar(B::P_FULL));
+        ++p_it;
+      }
+      if (!ok) break;
+      // Epilogue: wait for the last PV, normalise, store.
+      ok = bounded_wait_warp(bar(B::P_EMPTY), (p_it - 1) & 1, p, abort_flag,
+                             FRATTN_STATUS_WAIT_TIMEOUT | 0x32);
+      if (!ok) break;
+      tc_fence_after();
+      const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
+      TI* orow = static_cast<TI*>(p.out) + (static_cast<size_t>(row) * p.H + h) * D;
+#pragma unroll
+      for (int c = 0; c < D / 16; ++c) {
+        uint32_t r[16];
+        tmem_ld16(lane_addr + C::TMEM_O + c * 16, r);
+        tmem_ld_wait();
+        if (row_ok) {
+          uint4 w0, w1;
+          w0.x = pack2<TI>(__uint_as_float(r[0]) * inv_l, __uint_as_float(r[1]) * inv_l);
+          w0.y = pack2<TI>(__uint_as_float(r[2]) * inv_l, __uint_as_float(r[3]) * inv_l);
+          w0.z = pack2<TI>(__uint_as_float(r[4]) * inv_l, __uint_as_float(r[5]) * inv_l);
+          w0.w = pack2<TI>(__uint_as_float(r[6]) * inv_l, __uint_as_float(r[7]) * inv_l);
+          w1.x = pack2<TI>(__uint_as_float(r[8]) * inv_l, __uint_as_float(r[9]) * inv_l);
+          w1.y = pack2<TI>(__uint_as_float(r[10]) * inv_l, __uint_as_float(r[11]) * inv_l);
+          w1.z = pack2<TI>(__uint_as_float(r[12]) * inv_l, __uint_as_float(r[13]) * inv_l);
+          w1.w = pack2<TI>(__uint_as_float(r[14]) * inv_l, __uint_as_float(r[15]) * inv_l);
+          reinterpret_cast<uint4*>(orow + c * 16)[0] = w0;
+          reinterpret_cast<uint4*>(orow + c * 16)[1] = w1;
+        }
+      }
+      tc_fence_before();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ scheduler
+// One CTA of 1024 threads builds the work list from cu_seqlens (see the file
+// header). Long items come first (largest kv ranges first per segment order),
+// packed items after them.
+constexpr int kPrepThreads = 1024;
+
+__device__ __forceinline__ int block_exclusive_scan(int v, int* tmp, int* total) {
+  // Simple Hillis-Steele scan over kPrepThreads values in shared memory.
+  const int t = threadIdx.x;
+  tmp[t] = v;
+  __syncthreads();
+  for (int off = 1; off < kPrepThreads; off <<= 1) {
+    const int x = t >= off ? tmp[t - off] : 0;
+    __syncthreads();
+    tmp[t] += x;
+    __syncthreads();
+  }
+  const int incl = tmp[t];
+  *total = tmp[kPrepThreads - 1];
+  __syncthreads();
+  return incl - v;
+}
+
+template <typename TI, int D>
+__global__ void __launch_bounds__(kPrepThreads, 1)
+    build_worklist(const int32_t* __restrict__ cu, int nseg, int T, int H, WorkItem* items,
+                   int* header, TI* out, int32_t* status, float* pos_tab, int pos_rows,
+                   float theta) {
+  __shared__ int tmp[kPrepThreads];
+  const int tid = threadIdx.x;
+
+  // Validate cu_seqlens: non-decreasing, inside [0, T].
+  int bad = 0;
+  for (int s = tid; s <= nseg; s += kPrepThreads) {
+    const int a = cu[s];
+    if (a < 0 || a > T) bad = 1;
+    if (s < nseg && cu[s + 1] < a) bad = 1;
+  }
+  bad = __syncthreads_or(bad);
+  if (bad) {
+    if (tid == 0) {
+      header[0] = 0;
+      if (status) atomicCAS(reinterpret_cast<int*>(status), 0, FRATTN_STATUS_BAD_SEQLENS);
+    }
+    return;
+  }
+
+  // Rotary table for the (h, w)-position entry point: [P, D/4] cos, then sin.
+  if (pos_tab != nullptr) {
+    constexpr int Q4 = D / 4;
+    for (int e = tid; e < pos_rows * Q4; e += kPrepThreads) {
+      const int pos = e / Q4, i = e % Q4;
+      // inv_freq[i] = 1 / theta^(2i / (D/2)), evaluated in fp32 like torch does
+      const float inv = 1.0f / powf(theta, static_cast<float>(2 * i) / static_cast<float>(D / 2));
+      const float ang = static_cast<float>(pos) * inv;
+      float sv, cv;
+      sincosf(ang, &sv, &cv);
+      pos_tab[e] = cv;
+      pos_tab[static_cast<size_t>(pos_rows) * Q4 + e] = sv;
+    }
+  }
+
+  const int c_first = cu[0], c_last = cu[nseg];
+  // Zero rows not covered by any segment.
+  {
+    const size_t row_elems = static_cast<size_t>(H) * D;  // multiple of 8
+    const size_t n0 = static_cast<size_t>(c_first) * row_elems / 8;
+    const size_t n1 = static_cast<size_t>(T - c_last) * row_elems / 8;
+    uint4 z = make_uint4(0, 0, 0, 0);
+    uint4* o0 = reinterpret_cast<uint4*>(out);
+    uint4* o1 = reinterpret_cast<uint4*>(out + static_cast<size_t>(c_last) * row_elems);
+    for (size_t i = tid; i < n0; i += kPrepThreads) o0[i] = z;
+    for (size_t i = tid; i < n1; i += kPrepThreads) o1[i] = z;
+  }
+
+  int base = 0, total = 0;
+  // Long items.
+  for (int s0 = 0; s0 < nseg; s0 += kPrepThreads) {
+    const int s = s0 + tid;
+    int a = 0, b = 0, n = 0;
+    if (s < nseg) {
+      a = cu[s];
+      b = cu[s + 1];
+      if (b - a > kTileM) n = (b - a + kTileM - 1) / kTileM;
+    }
+    const int off = block_exclusive_scan(n, tmp, &total);
+    for (int i = 0; i < n; ++i) {
+      WorkItem w;
+      w.q0 = a + i * kTileM;
+      w.q1 = min(a + (i + 1) * kTileM, b);
+      w.kv0 = a;
+      w.kv1 = b;
+      w.seg_lo = s;
+      w.seg_hi = s;
+      w.kind = kItemLong;
+      w.pad = 0;
+      items[base + off + i] = w;
+    }
+    base += total;
+  }
+  // Packed items: per 128-row chunk, the rows of short segments inside it.
+  const int nch = (T + kTileM - 1) / kTileM;
+  for (int c0 = 0; c0 < nch; c0 += kPrepThreads) {
+    const int c = c0 + tid;
+    int has = 0;
+    WorkItem w;
+    if (c < nch && c_first < c_last) {
+      int a = max(c * kTileM, c_first);
+      int e = min(c * kTileM + kTileM, min(T, c_last));
+      if (a < e) {
+        int sa = upper_bound_cu(cu, 0, nseg + 1, a) - 1;
+        if (cu[sa + 1] - cu[sa] > kTileM) {
+          a = cu[sa + 1];
+          if (a < e) sa = upper_bound_cu(cu, 0, nseg + 1, a) - 1;
+        }
+        if (a < e && cu[sa + 1] - cu[sa] <= kTileM) {
+          int se = upper_bound_cu(cu, 0, nseg + 1, e - 1) - 1;
+          if (cu[se + 1] - cu[se] > kTileM) {
+            e = cu[se];
+            if (a < e) se = upper_bound_cu(cu, 0, nseg + 1, e - 1) - 1;
+          }
+          if (a < e) {
+            has = 1;
+            w.q0 = a;
+            w.q1 = e;
+            w.kv0 = cu[sa];
+            w.kv1 = cu[se + 1];
+            w.seg_lo = sa;
+            w.seg_hi = se;
+            w.kind = kItemPacked;
+            w.pad = 0;
+          }
+        }
+      }
+    }
+    const int off = block_exclusive_scan(has, tmp, &total);
+    if (has) items[base + off] = w;
+    base += total;
+  }
+  if (tid == 0) header[0] = base;
+}
+
+// Failure-path self test: wait on a barrier nothing arrives on.
+__global__ void wait_timeout_kernel(int32_t* status, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t b;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&b), 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  Params p;
+  memset(&p, 0, sizeof(p));
+  p.status = status;
+  p.wait_limit_ns = limit_ns;
+  bounded_wait(smem_u32(&b), 0, p, &abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0xF0);
+}
+
+}  // namespace frattn
+
+// ====================================================================== host
+using namespace frattn;
+
+namespace {
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+PFN_encodeTiled get_encode_fn() {
+  static PFN_encodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(f);
+  });
+  return fn;
+}
+
+unsigned long long g_wait_limit_ns = 2000000000ull;
+
+int sm_count_for_current_device() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+// [T, H, D] tensor viewed as 3-D {D, H, T}; box {16, 1, 128}, 32-B swizzle.
+int make_qkv_map(CUtensorMap* m, const void* base, int T, int H, int D, bool bf16) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (!enc) return FRATTN_E_TMAP;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(H),
+                        static_cast<cuuint64_t>(T)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(H) * D * 2};
+  cuuint32_t box[3] = {16, 1, static_cast<cuuint32_t>(kTileM)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : FRATTN_E_TMAP;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <int D, int MODE, typename TI, typename TC>
+int launch_attn(const Params& prm, cudaStream_t st) {
+  using C = Cfg<D>;
+  auto kern = fused_rope_attn_kernel<D, MODE, TI, TC>;
+  // Per-device flag; setting the attribute twice is harmless, so races are benign.
+  static unsigned long long attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(attr_set & bit)) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) !=
+        cudaSuccess)
+      return FRATTN_E_CUDA;
+    attr_set |= bit;
+  }
+  const int grid = sm_count_for_current_device();
+  kern<<<grid, kThreads, C::SMEM_BYTES, st>>>(prm);
+  return cudaGetLastError() == cudaSuccess ? 0 : FRATTN_E_CUDA;
+}
+
+template <int D, int MODE, typename TI>
+int dispatch_cs(const Params& prm, int cs_dtype, cudaStream_t st) {
+  if (MODE == kRopePos) return launch_attn<D, MODE, TI, float>(prm, st);
+  switch (cs_dtype) {
+    case FRATTN_F32: return launch_attn<D, MODE, TI, float>(prm, st);
+    case FRATTN_BF16: return launch_attn<D, MODE, TI, __nv_bfloat16>(prm, st);
+    case FRATTN_F16: return launch_attn<D, MODE, TI, __half>(prm, st);
+    default: return FRATTN_E_DTYPE;
+  }
+}
+
+template <int D, int MODE>
+int dispatch_in(const Params& prm, int in_dtype, int cs_dtype, cudaStream_t st) {
+  if (in_dtype == FRATTN_BF16) return dispatch_cs<D, MODE, __nv_bfloat16>(prm, cs_dtype, st);
+  if (in_dtype == FRATTN_F16) return dispatch_cs<D, MODE, __half>(prm, cs_dtype, st);
+  return FRATTN_E_DTYPE;
+}
+
+template <int MODE>
+int dispatch_d(const Params& prm, int D, int in_dtype, int cs_dtype, cudaStream_t st) {
+  switch (D) {
+    case 64: return dispatch_in<64, MODE>(prm, in_dtype, cs_dtype, st);
+    case 80: return dispatch_in<80, MODE>(prm, in_dtype, cs_dtype, st);
+    case 96: return dispatch_in<96, MODE>(prm, in_dtype, cs_dtype, st);
+    case 128: return dispatch_in<128, MODE>(prm, in_dtype, cs_dtype, st);
+    default: return FRATTN_E_SHAPE;
+  }
+}
+
+template <typename TI>
+int launch_prep_t(const int32_t* cu, int nseg, int T, int H, int D, WorkItem* items, int* header,
+                  void* out, int32_t* status, float* pos_tab, int pos_rows, float theta,
+                  cudaStream_t st) {
+  switch (D) {
+#define FRATTN_PREP_CASE(DD)                                                                    \
+  case DD:                                                                                      \
+    build_worklist<TI, DD><<<1, kPrepThreads, 0, st>>>(cu, nseg, T, H, items, header,           \
+                                                       static_cast<TI*>(out), status, pos_tab,  \
+                                                       pos_rows, theta);                        \
+    break;
+    FRATTN_PREP_CASE(64)
+    FRATTN_PREP_CASE(80)
+    FRATTN_PREP_CASE(96)
+    FRATTN_PREP_CASE(128)
+#undef FRATTN_PREP_CASE
+    default: return FRATTN_E_SHAPE;
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : FRATTN_E_CUDA;
+}
+
+size_t pos_table_bytes(int max_position, int D) {
+  return (static_cast<size_t>(max_position) * (D / 4) * 2 * sizeof(float) + 255) & ~size_t(255);
+}
+
+int common_checks(const void* q, const void* k, const void* v, const int32_t* cu, int nseg, int T,
+                  int H, int D, int in_dtype, void* out, void* ws) {
+  if (!q || !k || !v || !cu || !out || !ws) return FRATTN_E_NULL;
+  if (T < 0 || H <= 0 || nseg < 1) return FRATTN_E_SHAPE;
+  if (D != 64 && D != 80 && D != 96 && D != 128) return FRATTN_E_SHAPE;
+  if (in_dtype != FRATTN_BF16 && in_dtype != FRATTN_F16) return FRATTN_E_DTYPE;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !aligned16(ws))
+    return FRATTN_E_ALIGN;
+  if (static_cast<long long>(T) * H * D >= (1ll << 31)) return FRATTN_E_SHAPE;
+  return 0;
+}
+
+template <int MODE>
+int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const void* sin,
+             int cs_dtype, const int32_t* pos_hw, int max_position, float theta,
+             const int32_t* cu, int nseg, int T, int H, int D, int in_dtype, void* out,
+             void* workspace, size_t ws_bytes, int32_t* status, void* stream) {
+  int rc = common_checks(q, k, v, cu, nseg, T, H, D, in_dtype, out, workspace);
+  if (rc) return rc;
+  size_t need = 0;
+  if (MODE == kRopeTable) {
+    frattn_workspace_bytes(T, nseg, &need);
+    if (!cos || !sin) return FRATTN_E_NULL;
+    if (cs_dtype != FRATTN_F32 && cs_dtype != FRATTN_F16 && cs_dtype != FRATTN_BF16)
+      return FRATTN_E_DTYPE;
+    if (!aligned16(cos) || !aligned16(sin)) return FRATTN_E_ALIGN;
+  } else {
+    if (!pos_hw) return FRATTN_E_NULL;
+    if (max_position <= 0 || max_position > 65536) return FRATTN_E_SHAPE;
+    if (reinterpret_cast<uintptr_t>(pos_hw) & 7u) return FRATTN_E_ALIGN;
+    frattn_workspace_bytes_pos(T, nseg, max_position, D, &need);
+  }
+  if (ws_bytes < need) return FRATTN_E_WORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* header = reinterpret_cast<int*>(ws);
+  WorkItem* items = reinterpret_cast<WorkItem*>(ws + kHeaderBytes);
+  float* pos_tab = nullptr;
+  if (MODE == kRopePos) {
+    size_t base = kHeaderBytes + max_items(T) * sizeof(WorkItem);
+    base = (base + 255) & ~size_t(255);
+    pos_tab = reinterpret_cast<float*>(ws + base);
+  }
+  if (in_dtype == FRATTN_BF16)
+    rc = launch_prep_t<__nv_bfloat16>(cu, nseg, T, H, D, items, header, out, status, pos_tab,
+                                      max_position, theta, st);
+  else
+    rc = launch_prep_t<__half>(cu, nseg, T, H, D, items, header, out, status, pos_tab,
+                               max_position, theta, st);
+  if (rc) return rc;
+  if (T == 0) return 0;
+
+  Params prm;
+  memset(&prm, 0, sizeof(prm));
+  const bool bf16 = in_dtype == FRATTN_BF16;
+  if (make_qkv_map(&prm.tmq, q, T, H, D, bf16) || make_qkv_map(&prm.tmk, k, T, H, D, bf16) ||
+      make_qkv_map(&prm.tmv, v, T, H, D, bf16))
+    return FRATTN_E_TMAP;
+  prm.cos = cos;
+  prm.sin = sin;
+  prm.pos_hw = pos_hw;
+  prm.pos_tab = pos_tab;
+  prm.pos_rows = max_position;
+  prm.cu = cu;
+  prm.nseg = nseg;
+  prm.out = out;
+  prm.items = items;
+  prm.header = header;
+  prm.T = T;
+  prm.H = H;
+  prm.status = status;
+  prm.wait_limit_ns = g_wait_limit_ns;
+  return dispatch_d<MODE>(prm, D, in_dtype, cs_dtype, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int frattn_version(void) { return 100; }
+
+const char* frattn_error_string(int code) {
+  switch (code) {
+    case FRATTN_OK: return "ok";
+    case FRATTN_E_SHAPE: return "invalid shape (T, H, D or nseg)";
+    case FRATTN_E_DTYPE: return "unsupported element type";
+    case FRATTN_E_ALIGN: return "pointer not 16-byte aligned";
+    case FRATTN_E_NULL: return "required pointer is NULL";
+    case FRATTN_E_WORKSPACE: return "workspace too small";
+    case FRATTN_E_CUDA: return "CUDA launch error";
+    case FRATTN_E_TMAP: return "tensor map encoding failed";
+    case FRATTN_STATUS_BAD_SEQLENS: return "cu_seqlens is not non-decreasing within [0, T]";
+    default:
+      if ((code & 0xF00) == FRATTN_STATUS_WAIT_TIMEOUT) return "device wait timed out";
+      return "unknown error";
+  }
+}
+
+int frattn_workspace_bytes(int total_tokens, int num_segments, size_t* bytes) {
+  if (!bytes) return FRATTN_E_NULL;
+  if (total_tokens < 0 || num_segments < 1) return FRATTN_E_SHAPE;
+  *bytes = kHeaderBytes + max_items(total_tokens) * sizeof(WorkItem);
+  return 0;
+}
+
+int frattn_workspace_bytes_pos(int total_tokens, int num_segments, int max_position, int D,
+                               size_t* bytes) {
+  if (!bytes) return FRATTN_E_NULL;
+  if (total_tokens < 0 || num_segments < 1 || max_position <= 0 || max_position > 65536)
+    return FRATTN_E_SHAPE;
+  size_t base = kHeaderBytes + max_items(total_tokens) * sizeof(WorkItem);
+  base = (base + 255) & ~size_t(255);
+  *bytes = base + pos_table_bytes(max_position, D);
+  return 0;
+}
+
+int frattn_fwd(const void* q, const void* k, const void* v, const void* cos, const void* sin,
+               int cs_dtype, const int32_t* cu_seqlens, int nseg, int T, int H, int D,
+               int max_seqlen, int in_dtype, void* out, void* workspace, size_t workspace_bytes,
+               int32_t* status, void* stream) {
+  (void)max_seqlen;
+  return fwd_impl<kRopeTable>(q, k, v, cos, sin, cs_dtype, nullptr, 0, 0.f, cu_seqlens, nseg, T,
+                              H, D, in_dtype, out, workspace, workspace_bytes, status, stream);
+}
+
+int frattn_fwd_pos(const void* q, const void* k, const void* v, const int32_t* pos_hw,
+                   int max_position, float theta, const int32_t* cu_seqlens, int nseg, int T,
+                   int H, int D, int max_seqlen, int in_dtype, void* out, void* workspace,
+                   size_t workspace_bytes, int32_t* status, void* stream) {
+  (void)max_seqlen;
+  return fwd_impl<kRopePos>(q, k, v, nullptr, nullptr, FRATTN_F32, pos_hw, max_position, theta,
+                            cu_seqlens, nseg, T, H, D, in_dtype, out, workspace, workspace_bytes,
+                            status, stream);
+}
+
+int frattn_selftest_wait_timeout(int32_t* status, uint64_t limit_ns, void* stream) {
+  if (!status) return FRATTN_E_NULL;
+  wait_timeout_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(status, limit_ns);
+  return cudaGetLastError() == cudaSuccess ? 0 : FRATTN_E_CUDA;
+}
+
+int frattn_set_wait_limit_ns(uint64_t limit_ns) {
+  if (limit_ns == 0) return FRATTN_E_SHAPE;
+  g_wait_limit_ns = limit_ns;
+  return 0;
+}
+
+}  // extern "C"

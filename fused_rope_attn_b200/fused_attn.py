@@ -1,0 +1,326 @@
+"""Host side of the fused 2D-RoPE + varlen attention path.
+
+Mirrors the public interface of the reference module ``fused_attn.py``
+(sdan/fused-rope-attn):
+
+* ``compute_rope_2d``      — fused_attn.py:33-136 (2D rotary cos/sin tables, LRU cached)
+* ``fused_rope_attention`` — fused_attn.py:139-232 (same signature, argument meaning and
+  ``ValueError`` behaviour), launching the sm_100a kernels of ``libfrattn.so`` through
+  the C ABI instead of a Triton kernel
+* ``next_pow2``            — fused_attn.py:13-15
+
+Additions that keep the call a drop-in:
+
+* keyword ``max_seqlen`` is accepted and ignored: the on-device scheduler derives the
+  work list from ``cu_seqlens`` itself, so no ``.item()`` host sync is needed
+  (the reference syncs at fused_attn.py:211);
+* ``fused_rope_attention_pos`` takes integer (h, w) patch positions instead of
+  materialised cos/sin tables and evaluates the rotary angles in the kernel.
+"""
+from __future__ import annotations
+
+import threading
+from collections import OrderedDict
+
+import torch
+
+from . import _lib
+
+__all__ = [
+    "next_pow2",
+    "compute_rope_2d",
+    "rope_positions_2d",
+    "fused_rope_attention",
+    "fused_rope_attention_pos",
+    "last_status",
+    "SUPPORTED_HEAD_DIMS",
+]
+
+SUPPORTED_HEAD_DIMS = (64, 80, 96, 128)
+
+_DT = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
+
+
+def next_pow2(n: int) -> int:
+    """Smallest power of two >= n (1 for n <= 0); fused_attn.py:13-15."""
+    n = int(n)
+    if n <= 1:
+        return 1
+    return 1 << (n - 1).bit_length()
+
+
+# --------------------------------------------------------------------------- RoPE tables
+_ROPE_CACHE_MAX = 32
+_rope_cache: "OrderedDict[tuple, tuple[torch.Tensor, torch.Tensor]]" = OrderedDict()
+_rope_lock = threading.Lock()
+
+
+def _thw_list(grid_thw) -> list[tuple[int, int, int]]:
+    if isinstance(grid_thw, torch.Tensor):
+        rows = grid_thw.detach().to("cpu").tolist()
+    else:
+        rows = list(grid_thw)
+    return [(int(r[0]), int(r[1]), int(r[2])) for r in rows]
+
+
+def _device_key(device: torch.device) -> tuple:
+    if device.type == "cuda":
+        return ("cuda", device.index if device.index is not None else torch.cuda.current_device())
+    return (device.type, device.index)
+
+
+def rope_positions_2d(grid_thw, spatial_merge_size: int = 2, device=None) -> torch.Tensor:
+    """(h, w) patch coordinates of every token, int32 ``[T, 2]``, in merge order.
+
+    Tokens of one image are ordered by merge block (row-major over the
+    ``h/m x w/m`` block grid) and, inside a block, row-major over its ``m x m``
+    patches; frames of a clip repeat the same coordinates
+    (the ordering built at fused_attn.py:84-102).
+    """
+    m = int(spatial_merge_size)
+    out = []
+    for t, h, w in _thw_list(grid_thw):
+        if h % m or w % m:
+            raise ValueError(f"h and w must be divisible by spatial_merge_size={m}, got h={h} w={w}")
+        bh = torch.arange(h // m).view(-1, 1, 1, 1)
+        bw = torch.arange(w // m).view(1, -1, 1, 1)
+        ih = torch.arange(m).view(1, 1, -1, 1)
+        iw = torch.arange(m).view(1, 1, 1, -1)
+        hh = (bh * m + ih).expand(h // m, w // m, m, m).reshape(-1)
+        ww = (bw * m + iw).expand(h // m, w // m, m, m).reshape(-1)
+        hw = torch.stack([hh, ww], dim=1)
+        out.append(hw.repeat(t, 1) if t > 1 else hw)
+    pos = torch.cat(out, 0).to(torch.int32) if out else torch.zeros(0, 2, dtype=torch.int32)
+    return pos.to(device) if device is not None else pos
+
+
+def compute_rope_2d(
+    grid_thw,
+    head_dim: int,
+    spatial_merge_size: int,
+    theta: float,
+    device,
+    dtype,
+    window_idx: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """2D rotary tables ``(cos, sin)``, each ``[T, head_dim // 2]`` (fused_attn.py:33-136).
+
+    Rotary index ``i < head_dim/4`` rotates with the patch row ``h``, index
+    ``head_dim/4 + i`` with the patch column ``w``; both use
+    ``inv_freq[i] = 1 / theta^(2i / (head_dim/2))``. Angles are formed in fp32 and
+    the tables cast to ``dtype``. Results are cached (32 entries, LRU) per
+    (grid, head_dim, merge, theta, device, dtype). ``window_idx`` permutes merge
+    units (groups of ``merge^2`` tokens) into window order after the cache.
+    """
+    if head_dim <= 0 or head_dim % 4 != 0:
+        raise ValueError(f"head_dim must be divisible by 4, got {head_dim}")
+    device = torch.device(device)
+    thw = _thw_list(grid_thw)
+    merge = int(spatial_merge_size)
+    rd = head_dim // 2
+    key = (tuple(thw), int(head_dim), merge, float(theta), *_device_key(device), dtype)
+    with _rope_lock:
+        hit = _rope_cache.get(key)
+        if hit is not None:
+            _rope_cache.move_to_end(key)
+    if hit is None:
+        inv_freq = 1.0 / (theta ** (torch.arange(0, rd, 2, device=device, dtype=torch.float32) / rd))
+        pos = rope_positions_2d(thw, merge, device=device).float()
+        ang = torch.cat([pos[:, 0:1] * inv_freq[None, :], pos[:, 1:2] * inv_freq[None, :]], dim=-1)
+        hit = (ang.cos().to(dtype).contiguous(), ang.sin().to(dtype).contiguous())
+        with _rope_lock:
+            _rope_cache[key] = hit
+            _rope_cache.move_to_end(key)
+            while len(_rope_cache) > _ROPE_CACHE_MAX:
+                _rope_cache.popitem(last=False)
+    cos, sin = hit
+    if window_idx is not None:
+        mu = merge * merge
+        idx = window_idx.to(device=device, dtype=torch.long)
+        cos = cos.view(-1, mu, rd)[idx].reshape(-1, rd)
+        sin = sin.view(-1, mu, rd)[idx].reshape(-1, rd)
+    return cos.contiguous(), sin.contiguous()
+
+
+# --------------------------------------------------------------------------- op wrapper
+_status: dict[int, torch.Tensor] = {}
+
+
+def _status_word(device: torch.device) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    s = _status.get(idx)
+    if s is None:
+        s = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status[idx] = s
+    return s
+
+
+def last_status(device=None, reset: bool = True) -> int:
+    """Device status word of the kernels on ``device`` (0 = no device-side error).
+
+    Reading it synchronises with the device. Non-zero values are the
+    ``FRATTN_STATUS_*`` codes of include/frattn.h.
+    """
+    device = torch.device("cuda") if device is None else torch.device(device)
+    s = _status_word(device)
+    v = int(s.item())
+    if reset and v:
+        s.zero_()
+    return v
+
+
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
+def _check_qkv(q, k, v):
+    if q.device.type != "cuda":
+        raise ValueError(f"q must be on CUDA, got device={q.device}")
+    if q.shape != k.shape or q.shape != v.shape:
+        raise ValueError(f"q/k/v must have same shape, got q={tuple(q.shape)} k={tuple(k.shape)} v={tuple(v.shape)}")
+    if q.ndim != 3:
+        raise ValueError(f"q/k/v must be [total_seq, num_heads, head_dim], got q.ndim={q.ndim}")
+    total, heads, hd = (int(x) for x in q.shape)
+    if hd <= 0 or hd % 2 != 0:
+        raise ValueError(f"head_dim must be positive and even, got {hd}")
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError(f"q dtype must be float16 or bfloat16, got {q.dtype}")
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError(f"q/k/v must share dtype, got q={q.dtype} k={k.dtype} v={v.dtype}")
+    if k.device != q.device or v.device != q.device:
+        raise ValueError(f"q/k/v must share a device, got q={q.device} k={k.device} v={v.device}")
+    return total, heads, hd
+
+
+def _check_cu(cu_seqlens, device):
+    if cu_seqlens.ndim != 1 or cu_seqlens.numel() < 2:
+        raise ValueError(f"cu_seqlens must be 1D with length >= 2, got {tuple(cu_seqlens.shape)}")
+    cu = cu_seqlens
+    if cu.dtype != torch.int32:
+        cu = cu.to(torch.int32)
+    if cu.device != device:
+        cu = cu.to(device, non_blocking=True)
+    return cu.contiguous()
+
+
+def _check_out(out, q):
+    if out is None:
+        return torch.empty_like(q)
+    if out.shape != q.shape:
+        raise ValueError(f"out must have shape {tuple(q.shape)}, got {tuple(out.shape)}")
+    if out.dtype != q.dtype or out.device != q.device:
+        raise ValueError(f"out must match q dtype/device, got out={out.dtype}/{out.device} q={q.dtype}/{q.device}")
+    if not out.is_contiguous() or out.data_ptr() % 16:
+        raise ValueError("out must be contiguous and 16-byte aligned")
+    return out
+
+
+def _check_head_dim(hd):
+    if hd not in SUPPORTED_HEAD_DIMS:
+        raise ValueError(f"head_dim {hd} is not supported by the sm_100a kernel (supported: {SUPPORTED_HEAD_DIMS})")
+
+
+def fused_rope_attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    cu_seqlens: torch.Tensor,
+    *,
+    out: torch.Tensor | None = None,
+    max_seqlen: int | None = None,
+) -> torch.Tensor:
+    """Fused RoPE + windowed/varlen attention over packed ``cu_seqlens`` segments.
+
+    Same contract as the reference (fused_attn.py:139-232):
+
+    * ``q, k, v``: ``[total_seq, num_heads, head_dim]``, float16 or bfloat16, CUDA
+    * ``cos, sin``: ``[total_seq, head_dim // 2]`` (float32, float16 or bfloat16),
+      split-half (NeoX) rotary applied to Q and K inside the kernel
+    * ``cu_seqlens``: ``[num_windows + 1]`` cumulative lengths (cast to int32)
+    * ``out``: optional preallocated output of q's shape/dtype/device
+
+    Returns ``out`` with ``softmax(R(q) R(k)^T / sqrt(head_dim)) v`` per segment and
+    head. Rows outside ``[cu_seqlens[0], cu_seqlens[-1])`` are zero.
+    """
+    total, heads, hd = _check_qkv(q, k, v)
+    if cos.shape != (total, hd // 2) or sin.shape != (total, hd // 2):
+        raise ValueError(
+            f"cos/sin must be [total_seq, head_dim//2]={total, hd // 2}, got cos={tuple(cos.shape)} sin={tuple(sin.shape)}"
+        )
+    if cu_seqlens.ndim != 1 or cu_seqlens.numel() < 2:
+        raise ValueError(f"cu_seqlens must be 1D with length >= 2, got {tuple(cu_seqlens.shape)}")
+    if cos.dtype not in _DT:
+        raise ValueError(f"cos dtype must be float16, bfloat16 or float32, got {cos.dtype}")
+    if sin.dtype not in _DT:
+        raise ValueError(f"sin dtype must be float16, bfloat16 or float32, got {sin.dtype}")
+    if sin.dtype != cos.dtype:
+        sin = sin.to(cos.dtype)
+    _check_head_dim(hd)
+    q, k, v = (_aligned(t.contiguous()) for t in (q, k, v))
+    cos = _aligned(cos.to(q.device).contiguous())
+    sin = _aligned(sin.to(q.device).contiguous())
+    out = _check_out(out, q)
+    cu = _check_cu(cu_seqlens, q.device)
+    nseg = cu.numel() - 1
+    lib = _lib.load()
+    ws_bytes = _lib.workspace_bytes(total, nseg)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    with torch.cuda.device(q.device):
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+        rc = lib.frattn_fwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), cos.data_ptr(), sin.data_ptr(), _DT[cos.dtype],
+            cu.data_ptr(), nseg, total, heads, hd, int(max_seqlen or 0), _DT[q.dtype],
+            out.data_ptr(), ws.data_ptr(), ws_bytes, _status_word(q.device).data_ptr(), stream,
+        )
+    _lib.check(rc, "frattn_fwd")
+    return out
+
+
+def fused_rope_attention_pos(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    pos_hw: torch.Tensor,
+    cu_seqlens: torch.Tensor,
+    *,
+    theta: float = 10000.0,
+    max_position: int | None = None,
+    out: torch.Tensor | None = None,
+    max_seqlen: int | None = None,
+) -> torch.Tensor:
+    """Fused RoPE + varlen attention with the rotary angles built in the kernel.
+
+    ``pos_hw`` is int32 ``[total_seq, 2]`` holding each token's (h, w) patch
+    coordinate (``rope_positions_2d`` builds it; window-shuffle it like q/k/v).
+    Equivalent to ``fused_rope_attention`` with
+    ``compute_rope_2d(..., dtype=torch.float32)`` tables. ``max_position`` bounds
+    the coordinates (exclusive); when omitted it is read from ``pos_hw`` (one
+    host sync).
+    """
+    total, heads, hd = _check_qkv(q, k, v)
+    if pos_hw.shape != (total, 2):
+        raise ValueError(f"pos_hw must be [total_seq, 2]={total, 2}, got {tuple(pos_hw.shape)}")
+    if hd % 4 != 0:
+        raise ValueError(f"head_dim must be divisible by 4 for 2D RoPE, got {hd}")
+    _check_head_dim(hd)
+    pos = _aligned(pos_hw.to(device=q.device, dtype=torch.int32).contiguous())
+    if max_position is None:
+        max_position = int(pos.max().item()) + 1 if total > 0 else 1
+    q, k, v = (_aligned(t.contiguous()) for t in (q, k, v))
+    out = _check_out(out, q)
+    cu = _check_cu(cu_seqlens, q.device)
+    nseg = cu.numel() - 1
+    lib = _lib.load()
+    ws_bytes = _lib.workspace_bytes_pos(total, nseg, max_position, hd)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    with torch.cuda.device(q.device):
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+        rc = lib.frattn_fwd_pos(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), pos.data_ptr(), int(max_position), float(theta),
+            cu.data_ptr(), nseg, total, heads, hd, int(max_seqlen or 0), _DT[q.dtype],
+            out.data_ptr(), ws.data_ptr(), ws_bytes, _status_word(q.device).data_ptr(), stream,
+        )
+    _lib.check(rc, "frattn_fwd_pos")
+    return out

@@ -1,0 +1,122 @@
+/*
+ * frattn.h — C ABI of the B200 (sm_100a) fused 2D-RoPE + varlen attention
+ * forward kernel.
+ *
+ * Everything here takes plain device pointers, sizes and a CUDA stream handle
+ * passed as `void*` (a cudaStream_t / CUstream); no framework types cross the
+ * boundary. All entry points return 0 on success, a negative FRATTN_E* code for
+ * an invalid argument (nothing was launched), or a positive code for a launch or
+ * driver failure.
+ *
+ * Reference interface replaced (sdan/fused-rope-attn):
+ *   fused_attn.py:139-232  fused_rope_attention(q, k, v, cos, sin, cu_seqlens, *, out)
+ *                          -> frattn_fwd
+ *   fused_attn.py:33-136   compute_rope_2d(...) (cos/sin from (h, w) grid ids)
+ *                          -> frattn_fwd_pos takes the (h, w) ids directly
+ *   fused_attn.py:246-423  fused_attn_kernel (Triton) -> the sm_100a kernels
+ *                          launched by frattn_fwd / frattn_fwd_pos
+ */
+#ifndef FRATTN_H_
+#define FRATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types (values of the *_dtype arguments). */
+enum {
+  FRATTN_F32 = 0,
+  FRATTN_F16 = 1,
+  FRATTN_BF16 = 2
+};
+
+/* Return codes. */
+enum {
+  FRATTN_OK = 0,
+  FRATTN_E_SHAPE = -1,     /* bad T / H / D / nseg                          */
+  FRATTN_E_DTYPE = -2,     /* unsupported q/k/v or cos/sin element type     */
+  FRATTN_E_ALIGN = -3,     /* a pointer is not 16-byte aligned              */
+  FRATTN_E_NULL = -4,      /* a required pointer is NULL                    */
+  FRATTN_E_WORKSPACE = -5, /* workspace smaller than frattn_workspace_bytes */
+  FRATTN_E_CUDA = 1,       /* CUDA runtime / driver error at launch         */
+  FRATTN_E_TMAP = 2        /* cuTensorMapEncodeTiled rejected a descriptor  */
+};
+
+/* Device status word codes (written by the kernels into *status, first error
+ * wins; read it back after the stream has synchronised). */
+enum {
+  FRATTN_STATUS_OK = 0,
+  FRATTN_STATUS_WAIT_TIMEOUT = 0x100, /* | role << 4 | barrier group        */
+  FRATTN_STATUS_BAD_SEQLENS = 0x200   /* cu_seqlens not non-decreasing in [0,T] */
+};
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int frattn_version(void);
+
+/* Human-readable text for a return code or a device status code. */
+const char* frattn_error_string(int code);
+
+/* Bytes of device workspace frattn_fwd / frattn_fwd_pos need for `total_tokens`
+ * packed tokens split into `num_segments` cu_seqlens segments. The workspace
+ * holds the work list the on-device scheduler builds from cu_seqlens on every
+ * call (no host synchronisation). Replaces the reference's host-side
+ * `window_lens.max().item()` and grid computation (fused_attn.py:209-218). */
+int frattn_workspace_bytes(int total_tokens, int num_segments, size_t* bytes);
+
+/* Fused RoPE + varlen attention forward (fused_attn.py:139-232 semantics):
+ *   for every segment s = [cu[s], cu[s+1]) and head h:
+ *     O[s,h] = softmax(R(Q[s,h]) R(K[s,h])^T / sqrt(D)) V[s,h]
+ *   with R the rotate-half rotary embedding using cos/sin rows of the token:
+ *     x0' = x0 cos - x1 sin, x1' = x0 sin + x1 cos  (x0 = x[:D/2], x1 = x[D/2:]),
+ *   computed in fp32 and rounded to the q/k/v element type before the product.
+ *
+ *   q, k, v, out : [T, H, D] contiguous, element type in_dtype (F16 or BF16)
+ *   cos, sin     : [T, D/2] contiguous, element type cs_dtype (F32, F16, BF16)
+ *   cu_seqlens   : [nseg + 1] int32, non-decreasing, values in [0, T]
+ *   max_seqlen   : optional hint (<= 0: unknown); the kernel never needs it
+ *   workspace    : >= frattn_workspace_bytes(T, nseg) bytes of device memory
+ *   status       : device int32 (may be NULL); set non-zero on a device error
+ *   stream       : cudaStream_t the kernels are launched on
+ * Rows of `out` outside [cu[0], cu[nseg]) are written with zeros (this makes an
+ * all-empty cu_seqlens return zeros, matching fused_attn.py:212-213).
+ * Supported D: 64, 80, 96, 128.
+ */
+int frattn_fwd(const void* q, const void* k, const void* v, const void* cos, const void* sin,
+               int cs_dtype, const int32_t* cu_seqlens, int nseg, int T, int H, int D,
+               int max_seqlen, int in_dtype, void* out, void* workspace, size_t workspace_bytes,
+               int32_t* status, void* stream);
+
+/* Same operation with the 2D rotary angles generated in the kernel from integer
+ * (h, w) patch positions instead of materialised cos/sin tables
+ * (compute_rope_2d, fused_attn.py:77-116, without the dtype cast):
+ *   inv_freq[i] = theta^(-2i / (D/2)),  i < D/4
+ *   angle[t, i]        = pos_hw[t, 0] * inv_freq[i]   (i < D/4)
+ *   angle[t, D/4 + i]  = pos_hw[t, 1] * inv_freq[i]
+ *   pos_hw : [T, 2] int32, 0 <= value < 65536.
+ * The per-position cos/sin table lives in the workspace, so this entry point
+ * needs frattn_workspace_bytes_pos(...) bytes instead. */
+int frattn_workspace_bytes_pos(int total_tokens, int num_segments, int max_position, int D,
+                               size_t* bytes);
+int frattn_fwd_pos(const void* q, const void* k, const void* v, const int32_t* pos_hw,
+                   int max_position, float theta, const int32_t* cu_seqlens, int nseg, int T,
+                   int H, int D, int max_seqlen, int in_dtype, void* out, void* workspace,
+                   size_t workspace_bytes, int32_t* status, void* stream);
+
+/* Test hook for the bounded-wait failure path: launches one CTA that waits on
+ * an mbarrier nothing ever arrives on, with a `limit_ns` bound, and returns
+ * through *status (FRATTN_STATUS_WAIT_TIMEOUT | ...) without faulting or
+ * hanging the GPU. No counterpart in the reference (which has no failure
+ * detection). */
+int frattn_selftest_wait_timeout(int32_t* status, uint64_t limit_ns, void* stream);
+
+/* Upper bound (nanoseconds) of every mbarrier wait inside the kernels;
+ * default 2e9. A wait that exceeds it sets *status and the kernel returns. */
+int frattn_set_wait_limit_ns(uint64_t limit_ns);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FRATTN_H_ */
