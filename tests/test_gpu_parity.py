@@ -1,0 +1,191 @@
+"""CUDA path (through the C ABI) vs the CPU oracle on the same seeded inputs.
+
+Tolerance (bf16/fp16 outputs vs the fp32 unfused path): max-abs <= 2e-2 and
+mean-abs <= 2e-3 per call.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from fused_rope_attn_b200 import fused_rope_attention, fused_rope_attention_pos, last_status, rope_positions_2d
+from fused_rope_attn_b200.utils import get_window_index
+from gpu_cases import cu_case, grid_case, mixed_sides, rand_qkv
+from oracle import rope_attn_oracle as O
+
+pytestmark = pytest.mark.gpu
+MAX_ABS, MEAN_ABS = 2e-2, 2e-3
+DEV = "cuda"
+
+
+def run(q, k, v, cos, sin, cu, **kw):
+    out = fused_rope_attention(q.to(DEV), k.to(DEV), v.to(DEV), cos.to(DEV), sin.to(DEV), cu.to(DEV), **kw)
+    torch.cuda.synchronize()
+    assert last_status() == 0
+    return out
+
+
+def oracle(q, k, v, cos, sin, cu):
+    return O.rope_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                            cos.float().numpy(), sin.float().numpy(), cu.numpy())
+
+
+def assert_close(out, ref, max_abs=MAX_ABS, mean_abs=MEAN_ABS):
+    o = out.float().cpu().numpy()
+    assert np.isfinite(o).all()
+    err = np.abs(o - ref)
+    assert err.max() <= max_abs and err.mean() <= mean_abs, (float(err.max()), float(err.mean()))
+
+
+@pytest.mark.parametrize("name,grid,windowed", [
+    ("cfg1_448_windowed", [(1, 32, 32)], True),
+    ("cfg2a_896_windowed", [(1, 64, 64)], True),
+    ("cfg2b_896_full", [(1, 64, 64)], False),
+    ("truncated_22x30", [(1, 22, 30)], True),
+    ("clip_t2", [(2, 16, 24)], True),
+])
+def test_config_parity(name, grid, windowed):
+    case = grid_case(grid, windowed, seed=hash(name) % 1000)
+    assert_close(run(*case), oracle(*case))
+
+
+def test_cfg3_mixed_varlen_batch():
+    grid = [(1, s, s) for s in mixed_sides(0)]
+    case = grid_case(grid, True, seed=3)
+    assert_close(run(*case), oracle(*case))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("cs_dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_dtypes(dtype, cs_dtype):
+    case = cu_case([0, 64, 100, 300, 301, 429], H=3, dtype=dtype, cs_dtype=cs_dtype, seed=5)
+    assert_close(run(*case), oracle(*case))
+
+
+@pytest.mark.parametrize("D", [64, 80, 96, 128])
+def test_head_dims(D):
+    case = cu_case([0, 64, 128, 390, 400], H=2, D=D, seed=D)
+    assert_close(run(*case), oracle(*case))
+
+
+@pytest.mark.parametrize("cu_list", [
+    [0, 1],                                  # single token
+    [0, 127], [0, 128], [0, 129],            # around the long-segment threshold
+    [0, 255, 256, 257],                      # long, length-1, length-1
+    [0, 0, 64, 64, 64, 130, 130],            # empty segments
+    [0, 5, 9, 70, 71, 200, 330, 331, 459],   # ragged, segments crossing 128-row chunks
+    list(range(0, 1025, 1)),                 # 1024 length-1 segments
+    [0, 3000],                               # one long segment, partial last tile
+])
+def test_edge_segmentations(cu_list):
+    case = cu_case(cu_list, H=2, seed=len(cu_list))
+    assert_close(run(*case), oracle(*case))
+
+
+def test_rows_outside_segments_are_zero():
+    q, k, v, cos, sin, cu = cu_case([40, 104, 170], H=2, T=256, seed=9)
+    out = run(q, k, v, cos, sin, cu).float().cpu()
+    ref = oracle(q, k, v, cos, sin, cu)
+    assert (out[:40] == 0).all() and (out[170:] == 0).all()
+    assert_close(out, ref)
+
+
+def test_all_empty_returns_zeros():
+    q, k, v, cos, sin, _ = cu_case([0, 64], H=2, seed=1)
+    out = run(q, k, v, cos, sin, torch.tensor([0, 0, 0], dtype=torch.int32))
+    assert (out == 0).all()
+
+
+def test_many_heads_and_out_param():
+    q, k, v, cos, sin, cu = cu_case([0, 64, 192, 250], H=32, seed=11)
+    out = torch.full((250, 32, 80), float("nan"), dtype=torch.bfloat16, device=DEV)
+    res = run(q, k, v, cos, sin, cu, out=out, max_seqlen=128)
+    assert res.data_ptr() == out.data_ptr()
+    assert_close(out, oracle(q, k, v, cos, sin, cu))
+
+
+def test_noncontiguous_and_int64_cpu_cu():
+    q, k, v, cos, sin, cu = cu_case([0, 64, 128, 300], H=4, seed=12)
+    qt = q.transpose(0, 1).contiguous().transpose(0, 1)  # same values, non-contiguous
+    out = fused_rope_attention(qt.to(DEV), k.to(DEV), v.to(DEV), cos.to(DEV), sin.to(DEV), cu.to(torch.int64))
+    torch.cuda.synchronize()
+    assert_close(out, oracle(q, k, v, cos, sin, cu))
+
+
+def test_wrapper_value_errors():
+    q, k, v, cos, sin, cu = [t.to(DEV) for t in cu_case([0, 64], H=2, seed=1)]
+    with pytest.raises(ValueError):
+        fused_rope_attention(q, k[:32], v, cos, sin, cu)
+    with pytest.raises(ValueError):
+        fused_rope_attention(q[:, 0], k[:, 0], v[:, 0], cos, sin, cu)
+    with pytest.raises(ValueError):
+        fused_rope_attention(q, k, v, cos[:, :20], sin, cu)
+    with pytest.raises(ValueError):
+        fused_rope_attention(q, k, v, cos, sin, cu[:1])
+    with pytest.raises(ValueError):
+        fused_rope_attention(q.float(), k.float(), v.float(), cos, sin, cu)
+    with pytest.raises(ValueError):
+        fused_rope_attention(q, k.half(), v, cos, sin, cu)
+    with pytest.raises(ValueError):
+        fused_rope_attention(q, k, v, cos.double(), sin, cu)
+    with pytest.raises(ValueError):
+        fused_rope_attention(q, k, v, cos, sin, cu, out=torch.empty_like(q)[:10])
+    with pytest.raises(ValueError):
+        fused_rope_attention(q, k, v, cos, sin, cu, out=torch.empty_like(q, dtype=torch.float16))
+
+
+def test_bad_cu_seqlens_sets_status():
+    q, k, v, cos, sin, _ = [t.to(DEV) for t in cu_case([0, 64], H=2, seed=1)]
+    fused_rope_attention(q, k, v, cos, sin, torch.tensor([0, 50, 20, 64], dtype=torch.int32, device=DEV))
+    torch.cuda.synchronize()
+    assert last_status() == 0x200
+    assert last_status() == 0  # reset after reading
+
+
+def test_device_wait_timeout_is_reported_not_hung():
+    from fused_rope_attn_b200 import _lib
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    rc = _lib.load().frattn_selftest_wait_timeout(st.data_ptr(), 20_000_000, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(st.item()) & 0xF00 == _lib.STATUS_WAIT_TIMEOUT
+    # the context is still usable
+    case = cu_case([0, 64], H=1, seed=2)
+    assert_close(run(*case), oracle(*case))
+
+
+def test_position_entry_point_matches_tables():
+    grid = [(1, 22, 30), (2, 8, 8)]
+    widx, cu = get_window_index(grid)
+    pos = rope_positions_2d(grid).reshape(-1, 4, 2)[widx].reshape(-1, 2)
+    q, k, v, cos, sin, _ = grid_case(grid, True, H=4, seed=21)
+    out_pos = fused_rope_attention_pos(q.to(DEV), k.to(DEV), v.to(DEV), pos.to(DEV), cu.to(DEV), theta=10000.0)
+    torch.cuda.synchronize()
+    assert last_status() == 0
+    assert_close(out_pos, oracle(q, k, v, cos, sin, cu))
+    out_tab = run(q, k, v, cos, sin, cu)
+    assert (out_pos.float() - out_tab.float()).abs().max().item() <= 2e-2
+
+
+def test_deterministic():
+    case = grid_case([(1, 32, 32)], False, H=4, seed=4)
+    a = run(*case)
+    b = run(*case)
+    assert torch.equal(a, b)
+
+
+def test_reference_kernel_golden_vectors():
+    """Our kernel on the inputs the reference kernel was run on (fp16 cases)."""
+    K = np.load(os.path.join(GOLDEN, "golden_kernel.npz"))
+    for name in sorted({key.split("/")[0] for key in K.files}):
+        q, k, v = (torch.from_numpy(K[f"{name}/{t}"]) for t in "qkv")
+        if q.dtype == torch.float32:
+            q, k, v = q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16)
+        cos, sin = torch.from_numpy(K[f"{name}/cos"]), torch.from_numpy(K[f"{name}/sin"])
+        cu = torch.from_numpy(K[f"{name}/cu_seqlens"])
+        out = run(q, k, v, cos, sin, cu).float().cpu().numpy()
+        ref = K[f"{name}/out"].astype(np.float32)
+        err = np.abs(out - ref)
+        assert err.max() <= MAX_ABS and err.mean() <= MEAN_ABS, (name, err.max(), err.mean())
