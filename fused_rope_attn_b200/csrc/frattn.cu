@@ -21,8 +21,10 @@
 //   * One persistent CTA per SM walks (item, head) units. Warp roles:
 //       warp 0      TMA producer (Q, K, V tiles; 32-B swizzled, 16-column blocks)
 //       warp 1      tcgen05 MMA issuer + TMEM owner
-//       warps 2-3   RoPE: rotate the raw Q/K tiles in shared memory in place
+//       warps 2-3   RoPE: rotate the raw Q/K tiles in shared memory in place,
+//                   two tile rows per thread, loads of a batch issued up front
 //       warps 4-7   softmax + O correction + epilogue, one thread per q row
+//                   (row = TMEM lane = 32 * (warp % 4) + lane)
 //   * S = Q K^T (M=128, N=128, K=D) and O += P V (M=128, N=D, K=128) run on the
 //     5th-gen tensor cores with fp32 accumulators in TMEM (S double-buffered).
 //   * Every mbarrier wait is bounded; on timeout the kernel records a status
@@ -274,37 +276,69 @@ __device__ __forceinline__ void rope_coeffs(const Params& p, int row, int i0, fl
   }
 }
 
-// Rotate a raw 128 x D tile in shared memory in place (rotate-half RoPE,
-// fp32 math, one rounding to the element type, fused_attn.py:340-345).
-template <int D, int MODE, typename TI, typename TC>
-__device__ __forceinline__ void rope_tile(uint8_t* tile, int row0, const Params& p, int tid) {
+// Rotate row r of a raw 128 x D tile in shared memory in place (rotate-half
+// RoPE, fp32 math, one rounding to the element type, fused_attn.py:340-345).
+// All shared and global loads of the row are issued before any arithmetic so
+// their latencies overlap.
+// Rotate chunks [C0, C1) of NR tile rows (r0 + i * kRopeThreads) in place.
+// All shared and global loads of the batch are issued before any arithmetic so
+// that their latencies overlap (rotate-half RoPE in fp32, one rounding to the
+// element type, fused_attn.py:340-345).
+template <int D, int MODE, typename TI, typename TC, int NR, int C0, int C1>
+__device__ __forceinline__ void rope_rows_part(uint8_t* tile, int row0, const Params& p, int r0) {
   constexpr int NP = D / 16;  // pairs of 8-element chunks: chunk c <-> chunk c + NP
-  for (int u = tid; u < kTileM * NP; u += kRopeThreads) {
-    const int r = u & (kTileM - 1);
-    const int c = u >> 7;
-    const int row = row0 + r;
-    if (row >= p.T) continue;
-    uint4* pa = reinterpret_cast<uint4*>(tile + chunk_off(r, c));
-    uint4* pb = reinterpret_cast<uint4*>(tile + chunk_off(r, c + NP));
-    float x0[8], x1[8], cs[8], sn[8];
-    unpack8<TI>(*pa, x0);
-    unpack8<TI>(*pb, x1);
-    rope_coeffs<D, MODE, TC>(p, row, c * 8, cs, sn);
-    uint4 oa, ob;
-    uint32_t* wa = reinterpret_cast<uint32_t*>(&oa);
-    uint32_t* wb = reinterpret_cast<uint32_t*>(&ob);
+  constexpr int N = C1 - C0;
+  uint4 xa[NR][N], xb[NR][N];
+  float cs[NR][N][8], sn[NR][N][8];
 #pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      const float a0 = x0[e] * cs[e] - x1[e] * sn[e];
-      const float a1 = x0[e + 1] * cs[e + 1] - x1[e + 1] * sn[e + 1];
-      const float b0 = x0[e] * sn[e] + x1[e] * cs[e];
-      const float b1 = x0[e + 1] * sn[e + 1] + x1[e + 1] * cs[e + 1];
-      wa[e / 2] = pack2<TI>(a0, a1);
-      wb[e / 2] = pack2<TI>(b0, b1);
+  for (int i = 0; i < NR; ++i) {
+    const int r = r0 + i * kRopeThreads;
+#pragma unroll
+    for (int c = 0; c < N; ++c) {
+      xa[i][c] = *reinterpret_cast<const uint4*>(tile + chunk_off(r, C0 + c));
+      xb[i][c] = *reinterpret_cast<const uint4*>(tile + chunk_off(r, C0 + c + NP));
     }
-    *pa = oa;
-    *pb = ob;
   }
+#pragma unroll
+  for (int i = 0; i < NR; ++i) {
+    const int row = min(row0 + r0 + i * kRopeThreads, p.T - 1);  // rows >= T hold TMA zeros
+#pragma unroll
+    for (int c = 0; c < N; ++c) rope_coeffs<D, MODE, TC>(p, row, (C0 + c) * 8, cs[i][c], sn[i][c]);
+  }
+#pragma unroll
+  for (int i = 0; i < NR; ++i) {
+    const int r = r0 + i * kRopeThreads;
+#pragma unroll
+    for (int c = 0; c < N; ++c) {
+      float x0[8], x1[8];
+      unpack8<TI>(xa[i][c], x0);
+      unpack8<TI>(xb[i][c], x1);
+      uint4 oa, ob;
+      uint32_t* wa = reinterpret_cast<uint32_t*>(&oa);
+      uint32_t* wb = reinterpret_cast<uint32_t*>(&ob);
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const float a0 = x0[e] * cs[i][c][e] - x1[e] * sn[i][c][e];
+        const float a1 = x0[e + 1] * cs[i][c][e + 1] - x1[e + 1] * sn[i][c][e + 1];
+        const float b0 = x0[e] * sn[i][c][e] + x1[e] * cs[i][c][e];
+        const float b1 = x0[e + 1] * sn[i][c][e + 1] + x1[e + 1] * cs[i][c][e + 1];
+        wa[e / 2] = pack2<TI>(a0, a1);
+        wb[e / 2] = pack2<TI>(b0, b1);
+      }
+      *reinterpret_cast<uint4*>(tile + chunk_off(r, C0 + c)) = oa;
+      *reinterpret_cast<uint4*>(tile + chunk_off(r, C0 + c + NP)) = ob;
+    }
+  }
+}
+
+// Rotate the rows of a raw 128 x D tile owned by this rope thread.
+template <int D, int MODE, typename TI, typename TC>
+__device__ __forceinline__ void rope_tile(uint8_t* tile, int row0, const Params& p, int r0) {
+  constexpr int NP = D / 16;
+  constexpr int NR = kTileM / kRopeThreads;
+  constexpr int H1 = (NP + 1) / 2;
+  rope_rows_part<D, MODE, TI, TC, NR, 0, H1>(tile, row0, p, r0);
+  rope_rows_part<D, MODE, TI, TC, NR, H1, NP>(tile, row0, p, r0);
 }
 
 __device__ __forceinline__ int upper_bound_cu(const int32_t* cu, int lo, int hi, int x) {
@@ -525,7 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
     }
   } else {
     // ------------------------------------------------------------ softmax WG
-    const int t = threadIdx.x - 128;  // q row within the tile == TMEM lane
+    const int t = ((warp & 3) << 5) | lane;  // q row within the tile == TMEM lane
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const float sl2 = 1.4426950408889634f * rsqrtf(static_cast<float>(D));
     uint32_t s_it = 0, p_it = 0;
@@ -575,18 +609,27 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
           for (int i = 0; i < kTileN; ++i)
             if (i < lo_r || i >= hi_r) s[i] = -INFINITY;
         }
-        float mx = m;
+        float mxp[8];
 #pragma unroll
-        for (int i = 0; i < kTileN; ++i) mx = fmaxf(mx, s[i]);
+        for (int i = 0; i < 8; ++i) mxp[i] = fmaxf(s[i], s[i + 8]);
+#pragma unroll
+        for (int i = 16; i < kTileN; i += 8) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) mxp[e] = fmaxf(mxp[e], s[i + e]);
+        }
+        float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                         fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+        mx = fmaxf(mx, m);
         const float m_use = (mx == -INFINITY) ? 0.f : mx;
         const float alpha = ex2((m - m_use) * sl2);  // m == -inf -> 0
         const float mb = m_use * sl2;
-        float sum = 0.f;
+        float sp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int i = 0; i < kTileN; ++i) {
           s[i] = ex2(fmaf(s[i], sl2, -mb));
-          sum += s[i];
+          sp[i & 7] += s[i];
         }
+        const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
         l = l * alpha + sum;
         m = mx;
 
