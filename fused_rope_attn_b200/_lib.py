@@ -16,7 +16,8 @@ LIB_PATH = os.path.join(_HERE, "libfrattn.so")
 F32, F16, BF16 = 0, 1, 2
 
 OK = 0
-E_SHAPE, E_DTYPE, E_ALIGN, E_NULL, E_WORKSPACE = -1, -2, -3, -4, -5
+E_SHAPE, E_DTYPE, E_ALIGN, E_NULL, E_WORKSPACE, E_NOALLOC_LIMIT = -1, -2, -3, -4, -5, -6
+NOALLOC_MAX_TOKENS = 65536
 E_CUDA, E_TMAP = 1, 2
 STATUS_WAIT_TIMEOUT = 0x100
 STATUS_BAD_SEQLENS = 0x200
@@ -30,6 +31,7 @@ _SIGNATURES = {
     "frattn_workspace_bytes_pos": (_i, [_i, _i, _i, _i, ctypes.POINTER(_sz)]),
     "frattn_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _sz, _vp, _vp]),
     "frattn_fwd_pos": (_i, [_vp, _vp, _vp, _vp, _i, _f, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _sz, _vp, _vp]),
+    "frattn_fwd_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
     "frattn_selftest_wait_timeout": (_i, [_vp, _u64, _vp]),
     "frattn_set_wait_limit_ns": (_i, [_u64]),
 }

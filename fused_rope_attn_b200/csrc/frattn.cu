@@ -1083,6 +1083,32 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
 
 }  // namespace
 
+// ---------------------------------------------------------------- no-alloc variant
+// Work-list storage for frattn_fwd_noalloc: a fixed device array that every GPU
+// loading this library keeps until the process exits. It is large enough for
+// FRATTN_NOALLOC_MAX_TOKENS packed tokens.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[FRATTN_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {nullptr};
+
+// Device address of g_noalloc_scratch on the current device (the symbol's name
+// in host code is only a host-side handle). Resolved once per device.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FRATTN_E_CUDA;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return FRATTN_E_CUDA;
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+}  // namespace
+
 extern "C" {
 
 int frattn_version(void) { return 100; }
@@ -1097,6 +1123,8 @@ const char* frattn_error_string(int code) {
     case FRATTN_E_WORKSPACE: return "workspace too small";
     case FRATTN_E_CUDA: return "CUDA launch error";
     case FRATTN_E_TMAP: return "tensor map encoding failed";
+    case FRATTN_E_NOALLOC_LIMIT:
+      return "total_tokens exceeds FRATTN_NOALLOC_MAX_TOKENS for frattn_fwd_noalloc";
     case FRATTN_STATUS_BAD_SEQLENS: return "cu_seqlens is not non-decreasing within [0, T]";
     default:
       if ((code & 0xF00) == FRATTN_STATUS_WAIT_TIMEOUT) return "device wait timed out";
@@ -1145,6 +1173,26 @@ int frattn_selftest_wait_timeout(int32_t* status, uint64_t limit_ns, void* strea
   if (!status) return FRATTN_E_NULL;
   wait_timeout_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(status, limit_ns);
   return cudaGetLastError() == cudaSuccess ? 0 : FRATTN_E_CUDA;
+}
+
+int frattn_fwd_noalloc(const void* q, const void* k, const void* v, const void* cos,
+                       const void* sin, int cs_dtype, const int32_t* cu_seqlens, int nseg, int T,
+                       int H, int D, int max_seqlen, int in_dtype, void* out, int32_t* status,
+                       void* stream) {
+  (void)max_seqlen;
+  if (T < 0 || T > FRATTN_NOALLOC_MAX_TOKENS) return FRATTN_E_NOALLOC_LIMIT;
+  size_t need = 0;
+  int rc = frattn_workspace_bytes(T, nseg, &need);
+  if (rc) return rc;
+  if (need > FRATTN_NOALLOC_SCRATCH_BYTES) return FRATTN_E_NOALLOC_LIMIT;
+  void* ws = nullptr;
+  rc = noalloc_scratch(&ws);
+  if (rc) return rc;
+  // The scheduler kernel rewrites the header and every item it uses on each
+  // call, so nothing in the array has to be cleared first.
+  return fwd_impl<kRopeTable>(q, k, v, cos, sin, cs_dtype, nullptr, 0, 0.f, cu_seqlens, nseg, T,
+                              H, D, in_dtype, out, ws, FRATTN_NOALLOC_SCRATCH_BYTES, status,
+                              stream);
 }
 
 int frattn_set_wait_limit_ns(uint64_t limit_ns) {

@@ -41,6 +41,7 @@ enum {
   FRATTN_E_ALIGN = -3,     /* a pointer is not 16-byte aligned              */
   FRATTN_E_NULL = -4,      /* a required pointer is NULL                    */
   FRATTN_E_WORKSPACE = -5, /* workspace smaller than frattn_workspace_bytes */
+  FRATTN_E_NOALLOC_LIMIT = -6, /* T above FRATTN_NOALLOC_MAX_TOKENS (frattn_fwd_noalloc) */
   FRATTN_E_CUDA = 1,       /* CUDA runtime / driver error at launch         */
   FRATTN_E_TMAP = 2        /* cuTensorMapEncodeTiled rejected a descriptor  */
 };
@@ -104,6 +105,35 @@ int frattn_fwd_pos(const void* q, const void* k, const void* v, const int32_t* p
                    int max_position, float theta, const int32_t* cu_seqlens, int nseg, int T,
                    int H, int D, int max_seqlen, int in_dtype, void* out, void* workspace,
                    size_t workspace_bytes, int32_t* status, void* stream);
+
+/* Allocation-free variant of frattn_fwd (no counterpart in the reference).
+ *
+ * For callers that cannot allocate device memory at the point of the call: a
+ * host runtime whose allocator is owned by someone else (a plugin inside another
+ * framework with no access to its caching allocator), code running where
+ * cudaMalloc would synchronise the device or is forbidden (latency-critical
+ * serving loops, some embedded/FFI hosts), or bindings that only see raw
+ * pointers. The work list that frattn_fwd keeps in the caller's workspace lives
+ * instead in one fixed device array inside this library
+ * (FRATTN_NOALLOC_SCRATCH_BYTES per GPU, held until the process exits), so the
+ * caller passes only inputs, outputs and a stream. Nothing is allocated: no
+ * cudaMalloc / cudaFree and no allocating library routine.
+ *
+ * Limits and rules:
+ *   - T (total_tokens) <= FRATTN_NOALLOC_MAX_TOKENS, else FRATTN_E_NOALLOC_LIMIT;
+ *   - the first call on a device looks up the array's device address (once,
+ *     with that device current); make that first call before any stream
+ *     capture;
+ *   - every call on a device shares the one array: calls whose kernels overlap
+ *     on the GPU (e.g. on two streams without ordering) race and may produce
+ *     wrong output. Order such calls on one stream or use frattn_fwd.
+ * Arguments and results are otherwise those of frattn_fwd. */
+#define FRATTN_NOALLOC_MAX_TOKENS 65536
+#define FRATTN_NOALLOC_SCRATCH_BYTES 65536
+int frattn_fwd_noalloc(const void* q, const void* k, const void* v, const void* cos,
+                       const void* sin, int cs_dtype, const int32_t* cu_seqlens, int nseg, int T,
+                       int H, int D, int max_seqlen, int in_dtype, void* out, int32_t* status,
+                       void* stream);
 
 /* Test hook for the bounded-wait failure path: launches one CTA that waits on
  * an mbarrier nothing ever arrives on, with a `limit_ns` bound, and returns

@@ -78,3 +78,11 @@ def test_wrapper_rejects_cpu_tensors():
     q = torch.zeros(4, 1, 80, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="CUDA"):
         fused_rope_attention(q, q, q, torch.zeros(4, 40), torch.zeros(4, 40), torch.tensor([0, 4]))
+
+
+def test_noalloc_rejects_oversize_before_touching_the_gpu():
+    lib = _lib.load()
+    rc = lib.frattn_fwd_noalloc(16, 16, 16, 16, 16, _lib.F32, 16, 1, _lib.NOALLOC_MAX_TOKENS + 1, 2, 80, 0,
+                                _lib.BF16, 16, None, None)
+    assert rc == _lib.E_NOALLOC_LIMIT
+    assert "NOALLOC" in _lib.error_string(rc)
