@@ -11,22 +11,29 @@
 //
 // Design (B200-native, not a translation of the Triton program grid):
 //   * An on-device scheduler kernel (`build_worklist`) turns cu_seqlens into a
-//     list of 128-row work items in the workspace, so no host sync is needed:
-//       - "long" items: 128-row q tiles of segments longer than 128 tokens, each
-//         attending to its whole segment;
+//     work list in the workspace, so no host sync is needed:
+//       - "long" items: 256-row q ranges (two 128-row tiles) of segments longer
+//         than 128 tokens, attending to their whole segment;
 //       - "packed" items: the rows of all short (<= 128 token) segments that
-//         start inside one 128-row chunk of the packed sequence, batched into
-//         one M=128 tile with a per-row segment mask. Two 64-token windows
-//         therefore share one tensor-core tile instead of two half-empty ones.
-//   * One persistent CTA per SM walks (item, head) units. Warp roles:
-//       warp 0      TMA producer (Q, K, V tiles; 32-B swizzled, 16-column blocks)
-//       warp 1      tcgen05 MMA issuer + TMEM owner
-//       warps 2-3   RoPE: rotate the raw Q/K tiles in shared memory in place,
-//                   two tile rows per thread, loads of a batch issued up front
-//       warps 4-7   softmax + O correction + epilogue, one thread per q row
-//                   (row = TMEM lane = 32 * (warp % 4) + lane)
-//   * S = Q K^T (M=128, N=128, K=D) and O += P V (M=128, N=D, K=128) run on the
-//     5th-gen tensor cores with fp32 accumulators in TMEM (S double-buffered).
+//         lie in one 128-row chunk of the packed sequence, batched into one
+//         M=128 tile with a per-row segment mask (two 64-token windows share
+//         one tensor-core tile instead of two half-empty ones).
+//   * One persistent CTA per SM walks units. A unit fills two 128-row q "slots"
+//     A and B: two q tiles of one (segment, head) sharing every K/V tile (long
+//     items), or heads 2g and 2g+1 of one packed item. The softmax of one slot
+//     overlaps the tensor-core work of the other.
+//   * 512 threads = 4 warpgroups with a setmaxnreg register split:
+//       WG0  warp 0 TMA producer (Q, K, V tiles; 32-B swizzle, 16-column
+//            blocks), warp 1 tcgen05 MMA issuer + TMEM owner
+//       WG1  RoPE: rotates raw Q/K tiles in shared memory in place, one tile row
+//            per thread, loads of a batch issued up front
+//       WG2  softmax + O rescale + epilogue of slot A (row = TMEM lane)
+//       WG3  the same for slot B
+//   * S = Q K^T (M=128, N=128, K=D, both operands in smem) and O += P V
+//     (M=128, N=D, K=128, P read from TMEM where it overwrites S) run on the
+//     5th-gen tensor cores with fp32 accumulators in TMEM.
+//   * The exponent reference max only moves when the row max grows by > 2^8,
+//     so O is rescaled rarely.
 //   * Every mbarrier wait is bounded; on timeout the kernel records a status
 //     code and returns instead of hanging the GPU.
 #include <cuda.h>
@@ -47,8 +54,18 @@ namespace frattn {
 
 constexpr int kTileM = 128;   // q rows per tile (TMEM lanes)
 constexpr int kTileN = 128;   // kv rows per tile
-constexpr int kThreads = 256; // 8 warps
-constexpr int kRopeThreads = 64;
+constexpr int kThreads = 512; // 16 warps = 4 warpgroups
+constexpr int kRopeThreads = 128;
+
+#ifndef FRATTN_REG_CTRL
+#define FRATTN_REG_CTRL 80
+#endif
+#ifndef FRATTN_REG_ROPE
+#define FRATTN_REG_ROPE 80
+#endif
+#ifndef FRATTN_REG_SOFTMAX
+#define FRATTN_REG_SOFTMAX 176
+#endif
 constexpr int kSoftmaxThreads = 128;
 constexpr int kBlkBytes = kTileM * 32;  // one 16-column (32 B) block of a 128-row tile
 
@@ -85,45 +102,6 @@ struct Params {
   int T, H;
   int32_t* status;
   unsigned long long wait_limit_ns;
-};
-
-template <int D>
-struct Cfg {
-  static_assert(D % 16 == 0 && D >= 32 && D <= 128, "D must be a multiple of 16 in [32,128]");
-  static constexpr int KB = D / 16;                  // column blocks per row
-  static constexpr int TILE_BYTES = kTileM * D * 2;  // one 128 x D bf16 tile
-  static constexpr int STAGES = D <= 96 ? 3 : 2;
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = OFF_Q + 2 * TILE_BYTES;
-  static constexpr int OFF_V = OFF_K + STAGES * TILE_BYTES;
-  static constexpr int OFF_P = OFF_V + STAGES * TILE_BYTES;
-  static constexpr int P_BYTES = kTileM * kTileN * 2;
-  static constexpr int OFF_BAR = OFF_P + P_BYTES;
-  static constexpr int BAR_BYTES = 512;
-  static constexpr int SMEM_BYTES = OFF_BAR + BAR_BYTES + 1024;  // +1024 alignment slack
-  // TMEM columns: S0 [0,128), S1 [128,256), O [256, 256 + D)
-  static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t TMEM_S0 = 0;
-  static constexpr uint32_t TMEM_O = 256;
-};
-
-// barrier slots (each 8 bytes)
-template <int STAGES>
-struct Bars {
-  static constexpr int Q_FULL = 0;                 // [2]
-  static constexpr int Q_READY = 2;                // [2]
-  static constexpr int Q_EMPTY = 4;                // [2]
-  static constexpr int K_FULL = 6;                 // [STAGES]
-  static constexpr int K_READY = K_FULL + STAGES;  // [STAGES]
-  static constexpr int K_EMPTY = K_READY + STAGES;
-  static constexpr int V_FULL = K_EMPTY + STAGES;
-  static constexpr int V_EMPTY = V_FULL + STAGES;
-  static constexpr int S_FULL = V_EMPTY + STAGES;  // [2]
-  static constexpr int S_FREE = S_FULL + 2;        // [2]
-  static constexpr int P_FULL = S_FREE + 2;
-  static constexpr int P_EMPTY = P_FULL + 1;
-  static constexpr int DONE = P_EMPTY + 1;
-  static constexpr int COUNT = DONE + 1;
 };
 
 // ------------------------------------------------------------------ helpers
@@ -331,14 +309,26 @@ __device__ __forceinline__ void rope_rows_part(uint8_t* tile, int row0, const Pa
   }
 }
 
+// Rotate chunks [C0, NP) of the rows owned by this rope thread in batches of
+// BS chunks (table mode: 3 then 2 for D = 80; position mode gathers 16 table
+// values per chunk, so it works in smaller batches to stay inside its registers).
+template <int D, int MODE, typename TI, typename TC, int C0, int BS>
+__device__ __forceinline__ void rope_batches(uint8_t* tile, int row0, const Params& p, int r0) {
+  constexpr int NP = D / 16;
+  constexpr int NR = kTileM / kRopeThreads;
+  if constexpr (C0 < NP) {
+    constexpr int C1 = (C0 + BS < NP) ? C0 + BS : NP;
+    rope_rows_part<D, MODE, TI, TC, NR, C0, C1>(tile, row0, p, r0);
+    rope_batches<D, MODE, TI, TC, C1, BS>(tile, row0, p, r0);
+  }
+}
+
 // Rotate the rows of a raw 128 x D tile owned by this rope thread.
 template <int D, int MODE, typename TI, typename TC>
 __device__ __forceinline__ void rope_tile(uint8_t* tile, int row0, const Params& p, int r0) {
   constexpr int NP = D / 16;
-  constexpr int NR = kTileM / kRopeThreads;
-  constexpr int H1 = (NP + 1) / 2;
-  rope_rows_part<D, MODE, TI, TC, NR, 0, H1>(tile, row0, p, r0);
-  rope_rows_part<D, MODE, TI, TC, NR, H1, NP>(tile, row0, p, r0);
+  constexpr int BS = MODE == kRopeTable ? (D <= 80 ? (NP + 1) / 2 : 2) : 1;
+  rope_batches<D, MODE, TI, TC, 0, BS>(tile, row0, p, r0);
 }
 
 __device__ __forceinline__ int upper_bound_cu(const int32_t* cu, int lo, int hi, int x) {
@@ -351,15 +341,110 @@ __device__ __forceinline__ int upper_bound_cu(const int32_t* cu, int lo, int hi,
 }
 
 // ------------------------------------------------------------------ kernel
+// A unit of work: one or two 128-row q tiles ("slots" A and B) that the CTA
+// runs concurrently so that the softmax of one slot overlaps the tensor-core
+// work of the other.
+//   long item  (segment > 128 tokens): slots A/B = consecutive q tiles of one
+//              (segment, head); they share every K/V tile.
+//   packed item: slots A/B = heads 2g and 2g+1 of the same packed rows; each
+//              slot has its own K/V tiles.
+struct Unit {
+  int q0a, q1a, q0b, q1b;
+  int ha, hb;
+  int kv0, kv1, seg_lo, seg_hi, kind;
+  bool has_b, shared;
+};
+
+__device__ __forceinline__ Unit decode_unit(const Params& p, int u, int n_long) {
+  Unit U;
+  const int hp = (p.H + 1) >> 1;
+  WorkItem it;
+  if (u < n_long * p.H) {
+    it = p.items[u / p.H];
+    const int h = u % p.H;
+    U.q0a = it.q0;
+    U.q1a = min(it.q0 + kTileM, it.q1);
+    U.q0b = it.q0 + kTileM;
+    U.q1b = it.q1;
+    U.ha = U.hb = h;
+    U.has_b = U.q0b < U.q1b;
+    U.shared = true;
+  } else {
+    const int v = u - n_long * p.H;
+    it = p.items[n_long + v / hp];
+    const int g = v % hp;
+    U.q0a = U.q0b = it.q0;
+    U.q1a = U.q1b = it.q1;
+    U.ha = 2 * g;
+    U.hb = 2 * g + 1;
+    U.has_b = U.hb < p.H;
+    U.shared = false;
+  }
+  U.kv0 = it.kv0;
+  U.kv1 = it.kv1;
+  U.seg_lo = it.seg_lo;
+  U.seg_hi = it.seg_hi;
+  U.kind = it.kind;
+  return U;
+}
+
+template <int D>
+struct Cfg {
+  static_assert(D % 16 == 0 && D >= 32 && D <= 128, "D must be a multiple of 16 in [32,128]");
+  static constexpr int KB = D / 16;                  // 32-byte column blocks per row
+  static constexpr int TILE_BYTES = kTileM * D * 2;  // one 128 x D tile
+  static constexpr int STAGES = D <= 80 ? 3 : 2;     // K/V ring depth
+  static constexpr int QBUF = D <= 96 ? 2 : 1;       // Q buffers per slot
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + 2 * QBUF * TILE_BYTES;
+  static constexpr int OFF_V = OFF_K + STAGES * TILE_BYTES;
+  static constexpr int OFF_BAR = OFF_V + STAGES * TILE_BYTES;
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int SMEM_BYTES = OFF_BAR + BAR_BYTES + 1024;  // +1024 alignment slack
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  // TMEM columns: S/P of slot X at 128 X, O of slot X at 256 + 128 X.
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t TMEM_S = 0;
+  static constexpr uint32_t TMEM_O = 256;
+};
+
+template <int ST, int QB>
+struct Bars {
+  static constexpr int Q_FULL = 0;                   // [2][QB]
+  static constexpr int Q_READY = Q_FULL + 2 * QB;    // [2][QB]
+  static constexpr int Q_EMPTY = Q_READY + 2 * QB;   // [2][QB]
+  static constexpr int K_FULL = Q_EMPTY + 2 * QB;    // [ST]
+  static constexpr int K_READY = K_FULL + ST;
+  static constexpr int K_EMPTY = K_READY + ST;
+  static constexpr int V_FULL = K_EMPTY + ST;
+  static constexpr int V_EMPTY = V_FULL + ST;
+  static constexpr int S_FULL = V_EMPTY + ST;        // [2] S of slot X in TMEM
+  static constexpr int P_FULL = S_FULL + 2;          // [2] P of slot X in TMEM (S consumed)
+  static constexpr int O_FULL = P_FULL + 2;          // [2] last PV of the unit done
+  static constexpr int DONE = O_FULL + 2;
+  static constexpr int COUNT = DONE + 1;
+};
+
+// Register split (setmaxnreg): 128 x (REG_CTRL + REG_ROPE) + 256 x REG_SOFTMAX
+// must not exceed the 512 x 128 launch budget.
+constexpr uint32_t REG_CTRL = FRATTN_REG_CTRL;
+constexpr uint32_t REG_ROPE = FRATTN_REG_ROPE;
+constexpr uint32_t REG_SOFTMAX = FRATTN_REG_SOFTMAX;
+#ifndef FRATTN_REG_EXPERIMENT
+static_assert(128 * (REG_CTRL + REG_ROPE) + 256 * REG_SOFTMAX <= 512 * 128, "register split");
+#endif
+
 template <int D, int MODE, typename TI, typename TC>
 __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __grid_constant__ Params p) {
   using C = Cfg<D>;
-  using B = Bars<C::STAGES>;
   constexpr int ST = C::STAGES;
+  constexpr int QB = C::QBUF;
+  using B = Bars<ST, QB>;
   constexpr bool kBF16 = std::is_same<TI, __nv_bfloat16>::value;
   constexpr uint32_t IDESC_S = make_idesc_f16(kBF16, kTileM, kTileN, false);
   constexpr uint32_t IDESC_O = make_idesc_f16(kBF16, kTileM, D, true);
   constexpr uint32_t SW32 = 6;
+  static_assert(B::COUNT * 8 + 16 <= C::BAR_BYTES, "barrier area");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -369,17 +454,21 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
   auto bar = [&](int i) -> uint32_t { return bar0 + 8u * static_cast<uint32_t>(i); };
   Ctl* ctl = reinterpret_cast<Ctl*>(smem + C::OFF_BAR + 8 * B::COUNT);
   volatile int* abort_flag = &ctl->abort;
+  auto qbuf = [&](int x, int b) -> uint32_t { return C::OFF_Q + (x * QB + b) * C::TILE_BYTES; };
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(bar(B::Q_FULL + i), 1);
-      mbar_init(bar(B::Q_READY + i), kRopeThreads);
-      mbar_init(bar(B::Q_EMPTY + i), 1);
-      mbar_init(bar(B::S_FULL + i), 1);
-      mbar_init(bar(B::S_FREE + i), kSoftmaxThreads);
+    for (int x = 0; x < 2; ++x) {
+      for (int b = 0; b < QB; ++b) {
+        mbar_init(bar(B::Q_FULL + x * QB + b), 1);
+        mbar_init(bar(B::Q_READY + x * QB + b), kRopeThreads);
+        mbar_init(bar(B::Q_EMPTY + x * QB + b), 1);
+      }
+      mbar_init(bar(B::S_FULL + x), 1);
+      mbar_init(bar(B::P_FULL + x), kSoftmaxThreads);
+      mbar_init(bar(B::O_FULL + x), 1);
     }
     for (int i = 0; i < ST; ++i) {
       mbar_init(bar(B::K_FULL + i), 1);
@@ -388,8 +477,6 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
       mbar_init(bar(B::V_FULL + i), 1);
       mbar_init(bar(B::V_EMPTY + i), 1);
     }
-    mbar_init(bar(B::P_FULL), kSoftmaxThreads);
-    mbar_init(bar(B::P_EMPTY), 1);
     mbar_init(bar(B::DONE), 1);
     ctl->abort = 0;
     fence_mbar_init();
@@ -410,199 +497,233 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
   const uint32_t tmem = ctl->tmem_base;
 
   const int n_items = __ldg(p.header);
-  const int n_units = n_items * p.H;
+  const int n_long = __ldg(p.header + 1);
+  const int n_units = n_long * p.H + (n_items - n_long) * ((p.H + 1) >> 1);
+  const int wg = warp >> 2;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      uint32_t q_it = 0, k_it = 0, v_it = 0;
+  if (wg == 0) {
+    regs_dec<REG_CTRL>();
+    if (warp == 0 && lane == 0) {
+      // ---------------------------------------------------------- TMA producer
+      uint32_t q_it[2] = {0, 0}, k_it = 0, v_it = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-        const WorkItem it = p.items[u / p.H];
-        const int h = u % p.H;
-        const int nkv = (it.kv1 - it.kv0 + kTileN - 1) / kTileN;
-        {
-          const int qs = q_it & 1;
-          ok = bounded_wait(bar(B::Q_EMPTY + qs), ((q_it >> 1) & 1) ^ 1, p, abort_flag,
+        const Unit U = decode_unit(p, u, n_long);
+        const int ns = U.has_b ? 2 : 1;
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          if (x >= ns || !ok) break;
+          const int qs = q_it[x] % QB;
+          ok = bounded_wait(bar(B::Q_EMPTY + x * QB + qs), ((q_it[x] / QB) & 1) ^ 1, p, abort_flag,
                             FRATTN_STATUS_WAIT_TIMEOUT | 0x00);
           if (!ok) break;
-          mbar_arrive_expect_tx(bar(B::Q_FULL + qs), C::TILE_BYTES);
-          const uint32_t dst = sbase + C::OFF_Q + qs * C::TILE_BYTES;
+          const uint32_t fb = bar(B::Q_FULL + x * QB + qs);
+          mbar_arrive_expect_tx(fb, C::TILE_BYTES);
 #pragma unroll
           for (int b = 0; b < C::KB; ++b)
-            tma_load_3d(dst + b * kBlkBytes, &p.tmq, bar(B::Q_FULL + qs), 16 * b, h, it.q0);
-          ++q_it;
+            tma_load_3d(sbase + qbuf(x, qs) + b * kBlkBytes, &p.tmq, fb, 16 * b, x ? U.hb : U.ha,
+                        x ? U.q0b : U.q0a);
+          ++q_it[x];
         }
+        const int nkv = (U.kv1 - U.kv0 + kTileN - 1) / kTileN;
+        const int nk = U.shared ? 1 : ns;
         for (int j = 0; j < nkv && ok; ++j) {
-          const int row = it.kv0 + j * kTileN;
-          const int ks = k_it % ST;
-          ok = bounded_wait(bar(B::K_EMPTY + ks), ((k_it / ST) & 1) ^ 1, p, abort_flag,
-                            FRATTN_STATUS_WAIT_TIMEOUT | 0x01);
-          if (!ok) break;
-          mbar_arrive_expect_tx(bar(B::K_FULL + ks), C::TILE_BYTES);
-          const uint32_t kdst = sbase + C::OFF_K + ks * C::TILE_BYTES;
+          const int row = U.kv0 + j * kTileN;
 #pragma unroll
-          for (int b = 0; b < C::KB; ++b)
-            tma_load_3d(kdst + b * kBlkBytes, &p.tmk, bar(B::K_FULL + ks), 16 * b, h, row);
-          ++k_it;
-          const int vs = v_it % ST;
-          ok = bounded_wait(bar(B::V_EMPTY + vs), ((v_it / ST) & 1) ^ 1, p, abort_flag,
-                            FRATTN_STATUS_WAIT_TIMEOUT | 0x02);
-          if (!ok) break;
-          mbar_arrive_expect_tx(bar(B::V_FULL + vs), C::TILE_BYTES);
-          const uint32_t vdst = sbase + C::OFF_V + vs * C::TILE_BYTES;
-#pragma unroll
-          for (int b = 0; b < C::KB; ++b)
-            tma_load_3d(vdst + b * kBlkBytes, &p.tmv, bar(B::V_FULL + vs), 16 * b, h, row);
-          ++v_it;
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      uint32_t q_it = 0, k_it = 0, v_it = 0, s_it = 0, p_it = 0;
-      bool ok = true;
-      const uint32_t pbase = sbase + C::OFF_P;
-      auto issue_s = [&](uint32_t qaddr) -> bool {
-        const int ks = k_it % ST;
-        const int sb = s_it & 1;
-        if (!bounded_wait(bar(B::S_FREE + sb), ((s_it >> 1) & 1) ^ 1, p, abort_flag,
-                          FRATTN_STATUS_WAIT_TIMEOUT | 0x10))
-          return false;
-        if (!bounded_wait(bar(B::K_READY + ks), (k_it / ST) & 1, p, abort_flag,
-                          FRATTN_STATUS_WAIT_TIMEOUT | 0x11))
-          return false;
-        tc_fence_after();
-        const uint32_t kaddr = sbase + C::OFF_K + ks * C::TILE_BYTES;
-        const uint32_t d = tmem + C::TMEM_S0 + sb * kTileN;
-#pragma unroll
-        for (int kb = 0; kb < C::KB; ++kb) {
-          const uint64_t ad = make_sdesc(qaddr + kb * kBlkBytes, 16, 256, SW32);
-          const uint64_t bd = make_sdesc(kaddr + kb * kBlkBytes, 16, 256, SW32);
-          umma_ss(d, ad, bd, IDESC_S, kb > 0 ? 1u : 0u);
-        }
-        umma_commit(bar(B::K_EMPTY + ks));
-        umma_commit(bar(B::S_FULL + sb));
-        ++k_it;
-        ++s_it;
-        return true;
-      };
-      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-        const WorkItem it = p.items[u / p.H];
-        const int nkv = (it.kv1 - it.kv0 + kTileN - 1) / kTileN;
-        const int qs = q_it & 1;
-        ok = bounded_wait(bar(B::Q_READY + qs), (q_it >> 1) & 1, p, abort_flag,
-                          FRATTN_STATUS_WAIT_TIMEOUT | 0x12);
-        if (!ok) break;
-        const uint32_t qaddr = sbase + C::OFF_Q + qs * C::TILE_BYTES;
-        ok = issue_s(qaddr);
-        for (int j = 0; j < nkv && ok; ++j) {
-          if (j + 1 < nkv) {
-            ok = issue_s(qaddr);
+          for (int x = 0; x < 2; ++x) {
+            if (x >= nk || !ok) break;
+            const int hx = x ? U.hb : U.ha;
+            const int ks = k_it % ST;
+            ok = bounded_wait(bar(B::K_EMPTY + ks), ((k_it / ST) & 1) ^ 1, p, abort_flag,
+                              FRATTN_STATUS_WAIT_TIMEOUT | 0x01);
             if (!ok) break;
-          }
-          if (j + 1 == nkv) umma_commit(bar(B::Q_EMPTY + qs));  // all S MMAs of this Q issued
-          const int vs = v_it % ST;
-          ok = bounded_wait(bar(B::P_FULL), p_it & 1, p, abort_flag,
-                            FRATTN_STATUS_WAIT_TIMEOUT | 0x13);
-          if (!ok) break;
-          ok = bounded_wait(bar(B::V_FULL + vs), (v_it / ST) & 1, p, abort_flag,
-                            FRATTN_STATUS_WAIT_TIMEOUT | 0x14);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t vaddr = sbase + C::OFF_V + vs * C::TILE_BYTES;
+            mbar_arrive_expect_tx(bar(B::K_FULL + ks), C::TILE_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < kTileN / 16; ++kk) {
-            const uint64_t ad = make_sdesc(pbase + kk * kBlkBytes, 16, 256, SW32);
-            const uint64_t bd = make_sdesc(vaddr + kk * 512, kBlkBytes, 256, SW32);
-            umma_ss(tmem + C::TMEM_O, ad, bd, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+            for (int b = 0; b < C::KB; ++b)
+              tma_load_3d(sbase + C::OFF_K + ks * C::TILE_BYTES + b * kBlkBytes, &p.tmk,
+                          bar(B::K_FULL + ks), 16 * b, hx, row);
+            ++k_it;
+            const int vs = v_it % ST;
+            ok = bounded_wait(bar(B::V_EMPTY + vs), ((v_it / ST) & 1) ^ 1, p, abort_flag,
+                              FRATTN_STATUS_WAIT_TIMEOUT | 0x02);
+            if (!ok) break;
+            mbar_arrive_expect_tx(bar(B::V_FULL + vs), C::TILE_BYTES);
+#pragma unroll
+            for (int b = 0; b < C::KB; ++b)
+              tma_load_3d(sbase + C::OFF_V + vs * C::TILE_BYTES + b * kBlkBytes, &p.tmv,
+                          bar(B::V_FULL + vs), 16 * b, hx, row);
+            ++v_it;
           }
-          umma_commit(bar(B::V_EMPTY + vs));
-          umma_commit(bar(B::P_EMPTY));
-          ++v_it;
-          ++p_it;
         }
-        ++q_it;
       }
-      // Drain: wait until every issued MMA has completed before TMEM is freed.
-      umma_commit(bar(B::DONE));
-      bounded_wait(bar(B::DONE), 0, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x15);
+    } else if (warp == 1) {
+      // ---------------------------------------------------------- MMA issuer
+      if (lane == 0) {
+        uint32_t q_it[2] = {0, 0}, k_it = 0, v_it = 0, p_it[2] = {0, 0};
+        bool ok = true;
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+          const Unit U = decode_unit(p, u, n_long);
+          const int ns = U.has_b ? 2 : 1;
+          const int nk = U.shared ? 1 : ns;
+          const int nkv = (U.kv1 - U.kv0 + kTileN - 1) / kTileN;
+          int qs[2] = {0, 0};
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            if (x >= ns || !ok) break;
+            qs[x] = q_it[x] % QB;
+            ok = bounded_wait(bar(B::Q_READY + x * QB + qs[x]), (q_it[x] / QB) & 1, p, abort_flag,
+                              FRATTN_STATUS_WAIT_TIMEOUT | 0x10);
+          }
+          if (!ok) break;
+          uint32_t vprev[2] = {0, 0};
+          for (int j = 0; j <= nkv && ok; ++j) {
+#pragma unroll
+            for (int x = 0; x < 2; ++x) {
+              if (x >= ns || !ok) break;
+              const uint32_t s_col = tmem + C::TMEM_S + 128u * x;
+              if (j > 0) {
+                // O_x (+)= P_x(j-1) V(j-1); P is read from TMEM (it aliases S_x).
+                ok = bounded_wait(bar(B::P_FULL + x), p_it[x] & 1, p, abort_flag,
+                                  FRATTN_STATUS_WAIT_TIMEOUT | 0x11);
+                if (!ok) break;
+                ++p_it[x];
+                const uint32_t vi = vprev[x];
+                ok = bounded_wait(bar(B::V_FULL + vi % ST), (vi / ST) & 1, p, abort_flag,
+                                  FRATTN_STATUS_WAIT_TIMEOUT | 0x12);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t vaddr = sbase + C::OFF_V + (vi % ST) * C::TILE_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < kTileN / 16; ++kk) {
+                  const uint64_t bd = make_sdesc(vaddr + kk * 512, kBlkBytes, 256, SW32);
+                  umma_ts(tmem + C::TMEM_O + 128u * x, s_col + kk * 8, bd, IDESC_O,
+                          (j > 1 || kk > 0) ? 1u : 0u);
+                }
+                if (!U.shared || x == ns - 1) umma_commit(bar(B::V_EMPTY + vi % ST));
+                if (j == nkv) umma_commit(bar(B::O_FULL + x));
+              }
+              if (j < nkv) {
+                // S_x(j) = Q_x K(j)^T
+                const uint32_t ki = k_it + (U.shared ? 0 : x);
+                ok = bounded_wait(bar(B::K_READY + ki % ST), (ki / ST) & 1, p, abort_flag,
+                                  FRATTN_STATUS_WAIT_TIMEOUT | 0x13);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t qaddr = sbase + qbuf(x, qs[x]);
+                const uint32_t kaddr = sbase + C::OFF_K + (ki % ST) * C::TILE_BYTES;
+#pragma unroll
+                for (int kb = 0; kb < C::KB; ++kb) {
+                  const uint64_t ad = make_sdesc(qaddr + kb * kBlkBytes, 16, 256, SW32);
+                  const uint64_t bd = make_sdesc(kaddr + kb * kBlkBytes, 16, 256, SW32);
+                  umma_ss(s_col, ad, bd, IDESC_S, kb > 0 ? 1u : 0u);
+                }
+                umma_commit(bar(B::S_FULL + x));
+                if (!U.shared || x == ns - 1) umma_commit(bar(B::K_EMPTY + ki % ST));
+                if (j == nkv - 1) umma_commit(bar(B::Q_EMPTY + x * QB + qs[x]));
+                vprev[x] = v_it + (U.shared ? 0 : x);
+              }
+            }
+            if (j < nkv) {
+              k_it += nk;
+              v_it += nk;
+            }
+          }
+          ++q_it[0];
+          if (ns > 1) ++q_it[1];
+        }
+        // Drain: every issued MMA completes before TMEM is released.
+        umma_commit(bar(B::DONE));
+        bounded_wait(bar(B::DONE), 0, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x15);
+      }
+      __syncwarp();
     }
-    __syncwarp();
-  } else if (warp < 4) {
-    // ------------------------------------------------------------ RoPE warps
-    const int tid = threadIdx.x - 64;
-    uint32_t q_it = 0, k_it = 0;
+  } else if (wg == 1) {
+    // ------------------------------------------------------------ RoPE warpgroup
+    regs_dec<REG_ROPE>();
+    const int r = threadIdx.x - 128;
+    uint32_t q_it[2] = {0, 0}, k_it = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-      const WorkItem it = p.items[u / p.H];
-      const int nkv = (it.kv1 - it.kv0 + kTileN - 1) / kTileN;
-      const int qs = q_it & 1;
-      ok = bounded_wait(bar(B::Q_FULL + qs), (q_it >> 1) & 1, p, abort_flag,
-                        FRATTN_STATUS_WAIT_TIMEOUT | 0x20);
-      if (!ok) break;
-      rope_tile<D, MODE, TI, TC>(smem + C::OFF_Q + qs * C::TILE_BYTES, it.q0, p, tid);
-      fence_proxy_async_smem();
-      mbar_arrive(bar(B::Q_READY + qs));
-      ++q_it;
-      for (int j = 0; j < nkv; ++j) {
-        const int ks = k_it % ST;
-        ok = bounded_wait(bar(B::K_FULL + ks), (k_it / ST) & 1, p, abort_flag,
-                          FRATTN_STATUS_WAIT_TIMEOUT | 0x21);
+      const Unit U = decode_unit(p, u, n_long);
+      const int ns = U.has_b ? 2 : 1;
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        if (x >= ns || !ok) break;
+        const int qs = q_it[x] % QB;
+        ok = bounded_wait(bar(B::Q_FULL + x * QB + qs), (q_it[x] / QB) & 1, p, abort_flag,
+                          FRATTN_STATUS_WAIT_TIMEOUT | 0x20);
         if (!ok) break;
-        rope_tile<D, MODE, TI, TC>(smem + C::OFF_K + ks * C::TILE_BYTES, it.kv0 + j * kTileN, p, tid);
+        rope_tile<D, MODE, TI, TC>(smem + qbuf(x, qs), x ? U.q0b : U.q0a, p, r);
         fence_proxy_async_smem();
-        mbar_arrive(bar(B::K_READY + ks));
-        ++k_it;
+        mbar_arrive(bar(B::Q_READY + x * QB + qs));
+        ++q_it[x];
+      }
+      const int nkv = (U.kv1 - U.kv0 + kTileN - 1) / kTileN;
+      const int nk = U.shared ? 1 : ns;
+      for (int j = 0; j < nkv && ok; ++j) {
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          if (x >= nk || !ok) break;
+          const int ks = k_it % ST;
+          ok = bounded_wait(bar(B::K_FULL + ks), (k_it / ST) & 1, p, abort_flag,
+                            FRATTN_STATUS_WAIT_TIMEOUT | 0x21);
+          if (!ok) break;
+          rope_tile<D, MODE, TI, TC>(smem + C::OFF_K + ks * C::TILE_BYTES, U.kv0 + j * kTileN, p, r);
+          fence_proxy_async_smem();
+          mbar_arrive(bar(B::K_READY + ks));
+          ++k_it;
+        }
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax WG
-    const int t = ((warp & 3) << 5) | lane;  // q row within the tile == TMEM lane
+    // ------------------------------------------------------------ softmax WGs
+    regs_inc<REG_SOFTMAX>();
+    const int x = wg - 2;                      // slot
+    const int t = ((warp & 3) << 5) | lane;    // q row within the tile == TMEM lane
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const uint32_t s_addr = lane_addr + C::TMEM_S + 128u * x;
+    const uint32_t o_addr = lane_addr + C::TMEM_O + 128u * x;
     const float sl2 = 1.4426950408889634f * rsqrtf(static_cast<float>(D));
-    uint32_t s_it = 0, p_it = 0;
+    constexpr float kRescaleLog2 = 8.0f;  // move the reference max only when it grows by 2^8
+    uint32_t s_it = 0, o_it = 0;
     bool ok = true;
-    uint8_t* pbuf = smem + C::OFF_P;
     for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-      const WorkItem it = p.items[u / p.H];
-      const int h = u % p.H;
-      const int nkv = (it.kv1 - it.kv0 + kTileN - 1) / kTileN;
-      const int row = it.q0 + t;
-      const bool row_ok = row < it.q1;
+      const Unit U = decode_unit(p, u, n_long);
+      if (x == 1 && !U.has_b) continue;
+      const int h = x ? U.hb : U.ha;
+      const int q0x = x ? U.q0b : U.q0a;
+      const int q1x = x ? U.q1b : U.q1a;
+      const int nkv = (U.kv1 - U.kv0 + kTileN - 1) / kTileN;
+      const int row = q0x + t;
       int lo = 0, hi = 0;
-      if (row_ok) {
-        if (it.kind == kItemLong) {
-          lo = it.kv0;
-          hi = it.kv1;
+      if (row < q1x) {
+        if (U.kind == kItemLong) {
+          lo = U.kv0;
+          hi = U.kv1;
         } else {
-          const int s = upper_bound_cu(p.cu, it.seg_lo, it.seg_hi + 2, row) - 1;
+          const int s = upper_bound_cu(p.cu, U.seg_lo, U.seg_hi + 2, row) - 1;
           lo = __ldg(p.cu + s);
           hi = __ldg(p.cu + s + 1);
         }
       }
-      float m = -INFINITY, l = 0.f;
+      float m_ref = -INFINITY, l = 0.f;
       for (int j = 0; j < nkv; ++j) {
-        const int sb = s_it & 1;
-        ok = bounded_wait_warp(bar(B::S_FULL + sb), (s_it >> 1) & 1, p, abort_flag,
+        ok = bounded_wait_warp(bar(B::S_FULL + x), s_it & 1, p, abort_flag,
                                FRATTN_STATUS_WAIT_TIMEOUT | 0x30);
         if (!ok) break;
+        ++s_it;
         tc_fence_after();
         float s[kTileN];
 #pragma unroll
-        for (int c = 0; c < kTileN / 16; ++c) {
-          uint32_t r[16];
-          tmem_ld16(lane_addr + C::TMEM_S0 + sb * kTileN + c * 16, r);
+        for (int c = 0; c < kTileN / 32; ++c) {
+          uint32_t rr[32];
+          tmem_ld32(s_addr + c * 32, rr);
 #pragma unroll
-          for (int e = 0; e < 16; ++e) s[c * 16 + e] = __uint_as_float(r[e]);
+          for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(rr[e]);
         }
         tmem_ld_wait();
-        tc_fence_before();
-        mbar_arrive(bar(B::S_FREE + sb));
-        ++s_it;
 
-        const int c0 = it.kv0 + j * kTileN;
+        const int c0 = U.kv0 + j * kTileN;
         const int lo_r = lo - c0, hi_r = hi - c0;
         if (lo_r > 0 || hi_r < kTileN) {
 #pragma unroll
@@ -617,86 +738,78 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
 #pragma unroll
           for (int e = 0; e < 8; ++e) mxp[e] = fmaxf(mxp[e], s[i + e]);
         }
-        float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                         fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
-        mx = fmaxf(mx, m);
-        const float m_use = (mx == -INFINITY) ? 0.f : mx;
-        const float alpha = ex2((m - m_use) * sl2);  // m == -inf -> 0
-        const float mb = m_use * sl2;
+        const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                               fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+        // The exponent reference only moves when the running max grows by more
+        // than 2^8 (or is still -inf); the final 1/l uses the same reference,
+        // so the result is exact up to rounding.
+        float alpha = 1.f;
+        bool rescale = false;
+        if (mx > m_ref && (m_ref == -INFINITY || (mx - m_ref) * sl2 > kRescaleLog2)) {
+          alpha = (m_ref == -INFINITY) ? 0.f : ex2((m_ref - mx) * sl2);
+          rescale = l > 0.f;
+          m_ref = mx;
+        }
+        const float mb = (m_ref == -INFINITY ? 0.f : m_ref) * sl2;
+        // p = 2^(s*scale - ref), written as packed pairs over the first 64 TMEM
+        // columns of the S region (already consumed into registers), 32 at a time.
         float sp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int i = 0; i < kTileN; ++i) {
-          s[i] = ex2(fmaf(s[i], sl2, -mb));
-          sp[i & 7] += s[i];
+        for (int c = 0; c < kTileN / 32; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float p0 = ex2(fmaf(s[c * 32 + 2 * e], sl2, -mb));
+            const float p1 = ex2(fmaf(s[c * 32 + 2 * e + 1], sl2, -mb));
+            sp[(2 * e) & 7] += p0;
+            sp[(2 * e + 1) & 7] += p1;
+            pk[e] = pack2<TI>(p0, p1);
+          }
+          tmem_st16(s_addr + c * 16, pk);
         }
         const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
         l = l * alpha + sum;
-        m = mx;
-
-        // P buffer / O accumulator are free once PV of the previous tile is done.
-        if (j > 0) {
-          ok = bounded_wait_warp(bar(B::P_EMPTY), (p_it - 1) & 1, p, abort_flag,
-                                 FRATTN_STATUS_WAIT_TIMEOUT | 0x31);
-          if (!ok) break;
-          tc_fence_after();
-          if (__any_sync(0xffffffffu, alpha != 1.f)) {
+        // O holds PV(j-1) complete: S_FULL(j) was committed after it.
+        if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
-            for (int c = 0; c < (D + 15) / 16; ++c) {
-              uint32_t r[16];
-              tmem_ld16(lane_addr + C::TMEM_O + c * 16, r);
-              tmem_ld_wait();
+          for (int c = 0; c < D / 16; ++c) {
+            uint32_t rr[16];
+            tmem_ld16(o_addr + c * 16, rr);
+            tmem_ld_wait();
 #pragma unroll
-              for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-              tmem_st16(lane_addr + C::TMEM_O + c * 16, r);
-            }
-            tmem_st_wait();
+            for (int e = 0; e < 16; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
+            tmem_st16(o_addr + c * 16, rr);
           }
         }
-        // Write P (bf16/fp16) as the K-major A operand: [kv block][row][32 B].
-        const uint32_t sw = (t >> 2) & 1;
-#pragma unroll
-        for (int kk = 0; kk < kTileN / 16; ++kk) {
-          uint4 h0, h1;
-          h0.x = pack2<TI>(s[kk * 16 + 0], s[kk * 16 + 1]);
-          h0.y = pack2<TI>(s[kk * 16 + 2], s[kk * 16 + 3]);
-          h0.z = pack2<TI>(s[kk * 16 + 4], s[kk * 16 + 5]);
-          h0.w = pack2<TI>(s[kk * 16 + 6], s[kk * 16 + 7]);
-          h1.x = pack2<TI>(s[kk * 16 + 8], s[kk * 16 + 9]);
-          h1.y = pack2<TI>(s[kk * 16 + 10], s[kk * 16 + 11]);
-          h1.z = pack2<TI>(s[kk * 16 + 12], s[kk * 16 + 13]);
-          h1.w = pack2<TI>(s[kk * 16 + 14], s[kk * 16 + 15]);
-          uint8_t* rowp = pbuf + kk * kBlkBytes + t * 32;
-          *reinterpret_cast<uint4*>(rowp + (sw << 4)) = h0;
-          *reinterpret_cast<uint4*>(rowp + ((sw ^ 1) << 4)) = h1;
-        }
-        fence_proxy_async_smem();
+        tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(bar(B::P_FULL));
-        ++p_it;
+        mbar_arrive(bar(B::P_FULL + x));
       }
       if (!ok) break;
-      // Epilogue: wait for the last PV, normalise, store.
-      ok = bounded_wait_warp(bar(B::P_EMPTY), (p_it - 1) & 1, p, abort_flag,
+      // Epilogue: last PV of this slot done -> normalise and store the row.
+      ok = bounded_wait_warp(bar(B::O_FULL + x), o_it & 1, p, abort_flag,
                              FRATTN_STATUS_WAIT_TIMEOUT | 0x32);
       if (!ok) break;
+      ++o_it;
       tc_fence_after();
+      const bool store = lo < hi;
       const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
       TI* orow = static_cast<TI*>(p.out) + (static_cast<size_t>(row) * p.H + h) * D;
 #pragma unroll
       for (int c = 0; c < D / 16; ++c) {
-        uint32_t r[16];
-        tmem_ld16(lane_addr + C::TMEM_O + c * 16, r);
+        uint32_t rr[16];
+        tmem_ld16(o_addr + c * 16, rr);
         tmem_ld_wait();
-        if (row_ok) {
+        if (store) {
           uint4 w0, w1;
-          w0.x = pack2<TI>(__uint_as_float(r[0]) * inv_l, __uint_as_float(r[1]) * inv_l);
-          w0.y = pack2<TI>(__uint_as_float(r[2]) * inv_l, __uint_as_float(r[3]) * inv_l);
-          w0.z = pack2<TI>(__uint_as_float(r[4]) * inv_l, __uint_as_float(r[5]) * inv_l);
-          w0.w = pack2<TI>(__uint_as_float(r[6]) * inv_l, __uint_as_float(r[7]) * inv_l);
-          w1.x = pack2<TI>(__uint_as_float(r[8]) * inv_l, __uint_as_float(r[9]) * inv_l);
-          w1.y = pack2<TI>(__uint_as_float(r[10]) * inv_l, __uint_as_float(r[11]) * inv_l);
-          w1.z = pack2<TI>(__uint_as_float(r[12]) * inv_l, __uint_as_float(r[13]) * inv_l);
-          w1.w = pack2<TI>(__uint_as_float(r[14]) * inv_l, __uint_as_float(r[15]) * inv_l);
+          w0.x = pack2<TI>(__uint_as_float(rr[0]) * inv_l, __uint_as_float(rr[1]) * inv_l);
+          w0.y = pack2<TI>(__uint_as_float(rr[2]) * inv_l, __uint_as_float(rr[3]) * inv_l);
+          w0.z = pack2<TI>(__uint_as_float(rr[4]) * inv_l, __uint_as_float(rr[5]) * inv_l);
+          w0.w = pack2<TI>(__uint_as_float(rr[6]) * inv_l, __uint_as_float(rr[7]) * inv_l);
+          w1.x = pack2<TI>(__uint_as_float(rr[8]) * inv_l, __uint_as_float(rr[9]) * inv_l);
+          w1.y = pack2<TI>(__uint_as_float(rr[10]) * inv_l, __uint_as_float(rr[11]) * inv_l);
+          w1.z = pack2<TI>(__uint_as_float(rr[12]) * inv_l, __uint_as_float(rr[13]) * inv_l);
+          w1.w = pack2<TI>(__uint_as_float(rr[14]) * inv_l, __uint_as_float(rr[15]) * inv_l);
           reinterpret_cast<uint4*>(orow + c * 16)[0] = w0;
           reinterpret_cast<uint4*>(orow + c * 16)[1] = w1;
         }
@@ -755,6 +868,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
   if (bad) {
     if (tid == 0) {
       header[0] = 0;
+      header[1] = 0;
       if (status) atomicCAS(reinterpret_cast<int*>(status), 0, FRATTN_STATUS_BAD_SEQLENS);
     }
     return;
@@ -796,13 +910,13 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
     if (s < nseg) {
       a = cu[s];
       b = cu[s + 1];
-      if (b - a > kTileM) n = (b - a + kTileM - 1) / kTileM;
+      if (b - a > kTileM) n = (b - a + 2 * kTileM - 1) / (2 * kTileM);
     }
     const int off = block_exclusive_scan(n, tmp, &total);
     for (int i = 0; i < n; ++i) {
       WorkItem w;
-      w.q0 = a + i * kTileM;
-      w.q1 = min(a + (i + 1) * kTileM, b);
+      w.q0 = a + i * 2 * kTileM;
+      w.q1 = min(a + (i + 1) * 2 * kTileM, b);
       w.kv0 = a;
       w.kv1 = b;
       w.seg_lo = s;
@@ -813,6 +927,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
     }
     base += total;
   }
+  const int n_long = base;
   // Packed items: per 128-row chunk, the rows of short segments inside it.
   const int nch = (T + kTileM - 1) / kTileM;
   for (int c0 = 0; c0 < nch; c0 += kPrepThreads) {
@@ -852,7 +967,10 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
     if (has) items[base + off] = w;
     base += total;
   }
-  if (tid == 0) header[0] = base;
+  if (tid == 0) {
+    header[0] = base;
+    header[1] = n_long;
+  }
 }
 
 // Failure-path self test: wait on a barrier nothing arrives on.
