@@ -29,6 +29,7 @@ _SIGNATURES = {
     "frattn_error_string": (ctypes.c_char_p, [_i]),
     "frattn_workspace_bytes": (_i, [_i, _i, ctypes.POINTER(_sz)]),
     "frattn_workspace_bytes_pos": (_i, [_i, _i, _i, _i, ctypes.POINTER(_sz)]),
+    "frattn_workspace_bytes_rotated_k": (_i, [_i, _i, _i, ctypes.POINTER(_sz)]),
     "frattn_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _sz, _vp, _vp]),
     "frattn_fwd_pos": (_i, [_vp, _vp, _vp, _vp, _i, _f, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _sz, _vp, _vp]),
     "frattn_fwd_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
@@ -99,4 +100,12 @@ def workspace_bytes_pos(total_tokens: int, num_segments: int, max_position: int,
     check(load().frattn_workspace_bytes_pos(int(total_tokens), int(num_segments), int(max_position),
                                             int(head_dim), ctypes.byref(out)),
           "frattn_workspace_bytes_pos")
+    return int(out.value)
+
+
+def workspace_bytes_rotated_k(total_tokens: int, num_heads: int, head_dim: int) -> int:
+    out = ctypes.c_size_t(0)
+    check(load().frattn_workspace_bytes_rotated_k(int(total_tokens), int(num_heads), int(head_dim),
+                                                  ctypes.byref(out)),
+          "frattn_workspace_bytes_rotated_k")
     return int(out.value)

@@ -89,6 +89,9 @@ enum RopeMode : int { kRopeTable = 0, kRopePos = 1 };
 
 struct Params {
   CUtensorMap tmq, tmk, tmv;
+  CUtensorMap tmk_rot;      // rotated K in the workspace (long segments), when krot != nullptr
+  const void* k;            // [T, H, D] raw K
+  void* krot;               // [T, H, D] K rotated once, rows of long segments only
   const void* cos;          // [T, D/2] (table mode)
   const void* sin;
   const int32_t* pos_hw;    // [T, 2] (pos mode)
@@ -340,6 +343,53 @@ __device__ __forceinline__ int upper_bound_cu(const int32_t* cu, int lo, int hi,
   return lo;
 }
 
+// ------------------------------------------------------------------ K pre-rotation
+// Rows of segments longer than one tile are read by every q tile of their
+// segment: rotating those K rows once per call (instead of once per q tile in
+// the attention kernel) turns L/128 rotations of each K tile into one, at the
+// cost of reading K and writing the rotated copy once (HBM-bound, a few us).
+// Short segments keep the fully fused path (their K tiles are used once).
+// Same arithmetic as rope_rows_part: fp32 rotation, one rounding.
+template <int D, int MODE, typename TI, typename TC>
+__global__ void __launch_bounds__(256) rotate_k_long(const __grid_constant__ Params p) {
+  constexpr int NP = D / 16;
+  const int n_long = __ldg(p.header + 1);
+  const TI* kin = static_cast<const TI*>(p.k);
+  TI* kout = static_cast<TI*>(p.krot);
+  const int stride = gridDim.x * blockDim.x;
+  for (int i = 0; i < n_long; ++i) {
+    const WorkItem it = p.items[i];
+    const int total = (it.q1 - it.q0) * p.H * NP;
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+      const int c = e % NP;
+      const int rh = e / NP;
+      const int h = rh % p.H;
+      const int row = it.q0 + rh / p.H;
+      const size_t base = (static_cast<size_t>(row) * p.H + h) * D;
+      const uint4 ua = __ldg(reinterpret_cast<const uint4*>(kin + base + 8 * c));
+      const uint4 ub = __ldg(reinterpret_cast<const uint4*>(kin + base + D / 2 + 8 * c));
+      float x0[8], x1[8], cs[8], sn[8];
+      unpack8<TI>(ua, x0);
+      unpack8<TI>(ub, x1);
+      rope_coeffs<D, MODE, TC>(p, row, 8 * c, cs, sn);
+      uint4 oa, ob;
+      uint32_t* wa = reinterpret_cast<uint32_t*>(&oa);
+      uint32_t* wb = reinterpret_cast<uint32_t*>(&ob);
+#pragma unroll
+      for (int q = 0; q < 8; q += 2) {
+        const float a0 = x0[q] * cs[q] - x1[q] * sn[q];
+        const float a1 = x0[q + 1] * cs[q + 1] - x1[q + 1] * sn[q + 1];
+        const float b0 = x0[q] * sn[q] + x1[q] * cs[q];
+        const float b1 = x0[q + 1] * sn[q + 1] + x1[q + 1] * cs[q + 1];
+        wa[q / 2] = pack2<TI>(a0, a1);
+        wb[q / 2] = pack2<TI>(b0, b1);
+      }
+      *reinterpret_cast<uint4*>(kout + base + 8 * c) = oa;
+      *reinterpret_cast<uint4*>(kout + base + D / 2 + 8 * c) = ob;
+    }
+  }
+}
+
 // ------------------------------------------------------------------ kernel
 // A unit of work: one or two 128-row q tiles ("slots" A and B) that the CTA
 // runs concurrently so that the softmax of one slot overlaps the tensor-core
@@ -486,6 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
     tma_prefetch_desc(&p.tmq);
     tma_prefetch_desc(&p.tmk);
     tma_prefetch_desc(&p.tmv);
+    if (p.krot) tma_prefetch_desc(&p.tmk_rot);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
@@ -527,6 +578,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
         }
         const int nkv = (U.kv1 - U.kv0 + kTileN - 1) / kTileN;
         const int nk = U.shared ? 1 : ns;
+        const CUtensorMap* kmap = (U.shared && p.krot) ? &p.tmk_rot : &p.tmk;
         for (int j = 0; j < nkv && ok; ++j) {
           const int row = U.kv0 + j * kTileN;
 #pragma unroll
@@ -540,7 +592,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
             mbar_arrive_expect_tx(bar(B::K_FULL + ks), C::TILE_BYTES);
 #pragma unroll
             for (int b = 0; b < C::KB; ++b)
-              tma_load_3d(sbase + C::OFF_K + ks * C::TILE_BYTES + b * kBlkBytes, &p.tmk,
+              tma_load_3d(sbase + C::OFF_K + ks * C::TILE_BYTES + b * kBlkBytes, kmap,
                           bar(B::K_FULL + ks), 16 * b, hx, row);
             ++k_it;
             const int vs = v_it % ST;
@@ -668,7 +720,8 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
           ok = bounded_wait(bar(B::K_FULL + ks), (k_it / ST) & 1, p, abort_flag,
                             FRATTN_STATUS_WAIT_TIMEOUT | 0x21);
           if (!ok) break;
-          rope_tile<D, MODE, TI, TC>(smem + C::OFF_K + ks * C::TILE_BYTES, U.kv0 + j * kTileN, p, r);
+          if (!(U.shared && p.krot))  // long segments: K arrives pre-rotated
+            rope_tile<D, MODE, TI, TC>(smem + C::OFF_K + ks * C::TILE_BYTES, U.kv0 + j * kTileN, p, r);
           fence_proxy_async_smem();
           mbar_arrive(bar(B::K_READY + ks));
           ++k_it;
@@ -1065,6 +1118,10 @@ int launch_attn(const Params& prm, cudaStream_t st) {
     attr_set |= bit;
   }
   const int grid = sm_count_for_current_device();
+  if (prm.krot) {
+    rotate_k_long<D, MODE, TI, TC><<<2 * grid, 256, 0, st>>>(prm);
+    if (cudaGetLastError() != cudaSuccess) return FRATTN_E_CUDA;
+  }
   kern<<<grid, kThreads, C::SMEM_BYTES, st>>>(prm);
   return cudaGetLastError() == cudaSuccess ? 0 : FRATTN_E_CUDA;
 }
@@ -1182,6 +1239,14 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
   if (make_qkv_map(&prm.tmq, q, T, H, D, bf16) || make_qkv_map(&prm.tmk, k, T, H, D, bf16) ||
       make_qkv_map(&prm.tmv, v, T, H, D, bf16))
     return FRATTN_E_TMAP;
+  // Rotated-K buffer after the work list (and table) when the workspace has room.
+  const size_t krot_off = (need + 255) & ~size_t(255);
+  const size_t krot_bytes = static_cast<size_t>(T) * H * D * 2;
+  if (ws_bytes >= krot_off + krot_bytes) {
+    prm.krot = ws + krot_off;
+    if (make_qkv_map(&prm.tmk_rot, prm.krot, T, H, D, bf16)) return FRATTN_E_TMAP;
+  }
+  prm.k = k;
   prm.cos = cos;
   prm.sin = sin;
   prm.pos_hw = pos_hw;
@@ -1254,6 +1319,14 @@ int frattn_workspace_bytes(int total_tokens, int num_segments, size_t* bytes) {
   if (!bytes) return FRATTN_E_NULL;
   if (total_tokens < 0 || num_segments < 1) return FRATTN_E_SHAPE;
   *bytes = kHeaderBytes + max_items(total_tokens) * sizeof(WorkItem);
+  return 0;
+}
+
+int frattn_workspace_bytes_rotated_k(int total_tokens, int num_heads, int head_dim,
+                                     size_t* bytes) {
+  if (!bytes) return FRATTN_E_NULL;
+  if (total_tokens < 0 || num_heads <= 0 || head_dim <= 0) return FRATTN_E_SHAPE;
+  *bytes = 256 + static_cast<size_t>(total_tokens) * num_heads * head_dim * 2;
   return 0;
 }
 

@@ -265,7 +265,7 @@ def fused_rope_attention(
     cu = _check_cu(cu_seqlens, q.device)
     nseg = cu.numel() - 1
     lib = _lib.load()
-    ws_bytes = _lib.workspace_bytes(total, nseg)
+    ws_bytes = _lib.workspace_bytes(total, nseg) + _lib.workspace_bytes_rotated_k(total, heads, hd)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
@@ -313,7 +313,8 @@ def fused_rope_attention_pos(
     cu = _check_cu(cu_seqlens, q.device)
     nseg = cu.numel() - 1
     lib = _lib.load()
-    ws_bytes = _lib.workspace_bytes_pos(total, nseg, max_position, hd)
+    ws_bytes = (_lib.workspace_bytes_pos(total, nseg, max_position, hd)
+                + _lib.workspace_bytes_rotated_k(total, heads, hd))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream

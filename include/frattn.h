@@ -67,6 +67,16 @@ const char* frattn_error_string(int code);
  * `window_lens.max().item()` and grid computation (fused_attn.py:209-218). */
 int frattn_workspace_bytes(int total_tokens, int num_segments, size_t* bytes);
 
+/* Extra workspace bytes that enable the rotated-K path for long segments:
+ * pass workspace_bytes >= frattn_workspace_bytes(...) (or _pos) + this value
+ * and the K rows of segments longer than 128 tokens are rotated once per call
+ * into the workspace by a short pre-pass, instead of once per 128-row q tile
+ * inside the attention kernel. Short segments (windows) always rotate K in the
+ * attention kernel. A workspace of only the base size is valid and keeps every
+ * rotation inside the attention kernel. No counterpart in the reference (its
+ * kernel re-rotates K for every q block, fused_attn.py:365-390). */
+int frattn_workspace_bytes_rotated_k(int total_tokens, int num_heads, int head_dim, size_t* bytes);
+
 /* Fused RoPE + varlen attention forward (fused_attn.py:139-232 semantics):
  *   for every segment s = [cu[s], cu[s+1]) and head h:
  *     O[s,h] = softmax(R(Q[s,h]) R(K[s,h])^T / sqrt(D)) V[s,h]
