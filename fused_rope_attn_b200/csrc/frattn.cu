@@ -57,6 +57,9 @@ constexpr int kTileN = 128;   // kv rows per tile
 constexpr int kThreads = 512; // 16 warps = 4 warpgroups
 constexpr int kRopeThreads = 128;
 
+#ifndef FRATTN_POLY_OF_8
+#define FRATTN_POLY_OF_8 0  // pairs (of every 8) whose exp2 runs on the FMA pipe
+#endif
 #ifndef FRATTN_REG_CTRL
 #define FRATTN_REG_CTRL 80
 #endif
@@ -89,7 +92,8 @@ enum RopeMode : int { kRopeTable = 0, kRopePos = 1 };
 
 struct Params {
   CUtensorMap tmq, tmk, tmv;
-  CUtensorMap tmk_rot;      // rotated K in the workspace (long segments), when krot != nullptr
+  CUtensorMap tmk_rot;
+  CUtensorMap tmcos, tmsin; // [T, D/2] cos/sin tables, box {D/2, 128} (table mode)      // rotated K in the workspace (long segments), when krot != nullptr
   const void* k;            // [T, H, D] raw K
   void* krot;               // [T, H, D] K rotated once, rows of long segments only
   const void* cos;          // [T, D/2] (table mode)
@@ -145,6 +149,69 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// ---- packed fp32 pairs (Blackwell f32x2 instructions) and exp2 on the FMA pipe
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2_rm(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair of arguments on the FMA pipe (offloads the MUFU unit):
+//   n = floor(x) via a round-down add of 1.5 * 2^23, f = x - n in [0, 1),
+//   2^f by a cubic fitted here (Lawson-iterated least squares on Chebyshev
+//   nodes, max relative error 7.5e-5, below the bf16/fp16 rounding of P),
+//   then n is added to the exponent field. Arguments are clamped at -126 so
+//   masked (-inf) entries give (nearly) 0; results are exact enough for P and
+//   the row sums (2^-13.7 relative).
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  float x0, x1;
+  f2unpack(x, x0, x1);
+  x = f2pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+  const uint64_t magic = f2pack(kMagic, kMagic);
+  const uint64_t t = add2_rm(x, magic);           // floor(x) + magic, exactly
+  const uint64_t f = sub2(x, sub2(t, magic));     // x - floor(x)
+  uint64_t y = fma2(f2pack(0.0780244916677475f, 0.0780244916677475f), f,
+                    f2pack(0.22606723010540009f, 0.22606723010540009f));
+  y = fma2(y, f, f2pack(0.6958335041999817f, 0.6958335041999817f));
+  y = fma2(y, f, f2pack(0.9999251961708069f, 0.9999251961708069f));
+  float t0, t1, y0, y1;
+  f2unpack(t, t0, t1);
+  f2unpack(y, y0, y1);
+  // bits(t) << 23 == floor(x) << 23 (mod 2^32): the magic's low 9 bits are 0
+  const uint32_t r0 = __float_as_uint(y0) + (__float_as_uint(t0) << 23);
+  const uint32_t r1 = __float_as_uint(y1) + (__float_as_uint(t1) << 23);
+  return f2pack(__uint_as_float(r0), __uint_as_float(r1));
+}
+
 template <typename T>
 __device__ __forceinline__ float to_f32(T x);
 template <>
@@ -184,6 +251,22 @@ __device__ __forceinline__ void load8<__half>(const __half* src, float (&v)[8]) 
     const float2 f = __half22float2(h[i]);
     v[2 * i] = f.x;
     v[2 * i + 1] = f.y;
+  }
+}
+
+// Load 8 consecutive cos/sin values from shared memory as fp32.
+template <typename TC>
+__device__ __forceinline__ void load8_smem(const TC* src, float (&v)[8]) {
+  if constexpr (std::is_same<TC, float>::value) {
+    const float4 a = reinterpret_cast<const float4*>(src)[0];
+    const float4 b = reinterpret_cast<const float4*>(src)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 a = *reinterpret_cast<const uint4*>(src);
+    const TC* h = reinterpret_cast<const TC*>(&a);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = to_f32<TC>(h[i]);
   }
 }
 
@@ -266,7 +349,8 @@ __device__ __forceinline__ void rope_coeffs(const Params& p, int row, int i0, fl
 // that their latencies overlap (rotate-half RoPE in fp32, one rounding to the
 // element type, fused_attn.py:340-345).
 template <int D, int MODE, typename TI, typename TC, int NR, int C0, int C1>
-__device__ __forceinline__ void rope_rows_part(uint8_t* tile, int row0, const Params& p, int r0) {
+__device__ __forceinline__ void rope_rows_part(uint8_t* tile, int row0, const Params& p, int r0,
+                                               const uint8_t* cs_smem) {
   constexpr int NP = D / 16;  // pairs of 8-element chunks: chunk c <-> chunk c + NP
   constexpr int N = C1 - C0;
   uint4 xa[NR][N], xb[NR][N];
@@ -283,8 +367,18 @@ __device__ __forceinline__ void rope_rows_part(uint8_t* tile, int row0, const Pa
 #pragma unroll
   for (int i = 0; i < NR; ++i) {
     const int row = min(row0 + r0 + i * kRopeThreads, p.T - 1);  // rows >= T hold TMA zeros
+    if (MODE == kRopeTable && cs_smem != nullptr) {
+      // cos/sin rows of this tile staged in shared memory: [128][D/2] cos, then sin
+      const TC* cst = reinterpret_cast<const TC*>(cs_smem) + (r0 + i * kRopeThreads) * (D / 2);
 #pragma unroll
-    for (int c = 0; c < N; ++c) rope_coeffs<D, MODE, TC>(p, row, (C0 + c) * 8, cs[i][c], sn[i][c]);
+      for (int c = 0; c < N; ++c) {
+        load8_smem<TC>(cst + (C0 + c) * 8, cs[i][c]);
+        load8_smem<TC>(cst + kTileM * (D / 2) + (C0 + c) * 8, sn[i][c]);
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < N; ++c) rope_coeffs<D, MODE, TC>(p, row, (C0 + c) * 8, cs[i][c], sn[i][c]);
+    }
   }
 #pragma unroll
   for (int i = 0; i < NR; ++i) {
@@ -316,22 +410,23 @@ __device__ __forceinline__ void rope_rows_part(uint8_t* tile, int row0, const Pa
 // BS chunks (table mode: 3 then 2 for D = 80; position mode gathers 16 table
 // values per chunk, so it works in smaller batches to stay inside its registers).
 template <int D, int MODE, typename TI, typename TC, int C0, int BS>
-__device__ __forceinline__ void rope_batches(uint8_t* tile, int row0, const Params& p, int r0) {
+__device__ __forceinline__ void rope_batches(uint8_t* tile, int row0, const Params& p, int r0,
+                                             const uint8_t* cs_smem) {
   constexpr int NP = D / 16;
   constexpr int NR = kTileM / kRopeThreads;
   if constexpr (C0 < NP) {
     constexpr int C1 = (C0 + BS < NP) ? C0 + BS : NP;
-    rope_rows_part<D, MODE, TI, TC, NR, C0, C1>(tile, row0, p, r0);
-    rope_batches<D, MODE, TI, TC, C1, BS>(tile, row0, p, r0);
+    rope_rows_part<D, MODE, TI, TC, NR, C0, C1>(tile, row0, p, r0, cs_smem);
+    rope_batches<D, MODE, TI, TC, C1, BS>(tile, row0, p, r0, cs_smem);
   }
 }
 
 // Rotate the rows of a raw 128 x D tile owned by this rope thread.
 template <int D, int MODE, typename TI, typename TC>
-__device__ __forceinline__ void rope_tile(uint8_t* tile, int row0, const Params& p, int r0) {
-  constexpr int NP = D / 16;
-  constexpr int BS = MODE == kRopeTable ? (D <= 80 ? (NP + 1) / 2 : 2) : 1;
-  rope_batches<D, MODE, TI, TC, 0, BS>(tile, row0, p, r0);
+__device__ __forceinline__ void rope_tile(uint8_t* tile, int row0, const Params& p, int r0,
+                                          const uint8_t* cs_smem = nullptr) {
+  constexpr int BS = 1;  // one chunk pair per batch: the rope warpgroup runs on 64 registers
+  rope_batches<D, MODE, TI, TC, 0, BS>(tile, row0, p, r0, cs_smem);
 }
 
 __device__ __forceinline__ int upper_bound_cu(const int32_t* cu, int lo, int hi, int x) {
@@ -356,15 +451,19 @@ __global__ void __launch_bounds__(256) rotate_k_long(const __grid_constant__ Par
   const int n_long = __ldg(p.header + 1);
   const TI* kin = static_cast<const TI*>(p.k);
   TI* kout = static_cast<TI*>(p.krot);
-  const int stride = gridDim.x * blockDim.x;
-  for (int i = 0; i < n_long; ++i) {
-    const WorkItem it = p.items[i];
-    const int total = (it.q1 - it.q0) * p.H * NP;
-    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
-      const int c = e % NP;
-      const int rh = e / NP;
+  // One flat index space over all long items (each covers at most 256 rows).
+  const int per_item = 2 * kTileM * p.H * NP;
+  const long long total = static_cast<long long>(n_long) * per_item;
+  for (long long e = blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += static_cast<long long>(gridDim.x) * blockDim.x) {
+    {
+      const int i = static_cast<int>(e / per_item);
+      const int rem = static_cast<int>(e % per_item);
+      const int c = rem % NP;
+      const int rh = rem / NP;
       const int h = rh % p.H;
-      const int row = it.q0 + rh / p.H;
+      const int row = __ldg(&p.items[i].q0) + rh / p.H;
+      if (row >= __ldg(&p.items[i].q1)) continue;
       const size_t base = (static_cast<size_t>(row) * p.H + h) * D;
       const uint4 ua = __ldg(reinterpret_cast<const uint4*>(kin + base + 8 * c));
       const uint4 ub = __ldg(reinterpret_cast<const uint4*>(kin + base + D / 2 + 8 * c));
@@ -438,18 +537,25 @@ __device__ __forceinline__ Unit decode_unit(const Params& p, int u, int n_long) 
   return U;
 }
 
-template <int D>
+template <int D, int CSB>
 struct Cfg {
   static_assert(D % 16 == 0 && D >= 32 && D <= 128, "D must be a multiple of 16 in [32,128]");
   static constexpr int KB = D / 16;                  // 32-byte column blocks per row
   static constexpr int TILE_BYTES = kTileM * D * 2;  // one 128 x D tile
-  static constexpr int STAGES = D <= 80 ? 3 : 2;     // K/V ring depth
-  static constexpr int QBUF = D <= 96 ? 2 : 1;       // Q buffers per slot
+  // cos/sin rows of the current unit staged in smem (table mode): [128][D/2] x 2
+  static constexpr int CS_BYTES = 2 * kTileM * (D / 2) * CSB;
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int kBudget = 232448 - BAR_BYTES - 1024;
+  static constexpr bool fits(int qb, int st) {
+    return (2 * qb + 2 * st) * TILE_BYTES + CS_BYTES <= kBudget;
+  }
+  static constexpr int STAGES = fits(1, D <= 80 ? 3 : 2) ? (D <= 80 ? 3 : 2) : 1;  // K/V ring
+  static constexpr int QBUF = fits(2, STAGES) ? 2 : 1;                             // Q per slot
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + 2 * QBUF * TILE_BYTES;
   static constexpr int OFF_V = OFF_K + STAGES * TILE_BYTES;
-  static constexpr int OFF_BAR = OFF_V + STAGES * TILE_BYTES;
-  static constexpr int BAR_BYTES = 512;
+  static constexpr int OFF_CS = OFF_V + STAGES * TILE_BYTES;
+  static constexpr int OFF_BAR = OFF_CS + ((CS_BYTES + 1023) & ~1023);
   static constexpr int SMEM_BYTES = OFF_BAR + BAR_BYTES + 1024;  // +1024 alignment slack
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
   // TMEM columns: S/P of slot X at 128 X, O of slot X at 256 + 128 X.
@@ -471,7 +577,9 @@ struct Bars {
   static constexpr int S_FULL = V_EMPTY + ST;        // [2] S of slot X in TMEM
   static constexpr int P_FULL = S_FULL + 2;          // [2] P of slot X in TMEM (S consumed)
   static constexpr int O_FULL = P_FULL + 2;          // [2] last PV of the unit done
-  static constexpr int DONE = O_FULL + 2;
+  static constexpr int CS_FULL = O_FULL + 2;          // cos/sin of the unit staged
+  static constexpr int CS_EMPTY = CS_FULL + 1;         // ... and no longer needed
+  static constexpr int DONE = CS_EMPTY + 1;
   static constexpr int COUNT = DONE + 1;
 };
 
@@ -486,7 +594,7 @@ static_assert(128 * (REG_CTRL + REG_ROPE) + 256 * REG_SOFTMAX <= 512 * 128, "reg
 
 template <int D, int MODE, typename TI, typename TC>
 __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __grid_constant__ Params p) {
-  using C = Cfg<D>;
+  using C = Cfg<D, MODE == kRopeTable ? static_cast<int>(sizeof(TC)) : 0>;
   constexpr int ST = C::STAGES;
   constexpr int QB = C::QBUF;
   using B = Bars<ST, QB>;
@@ -527,6 +635,8 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
       mbar_init(bar(B::V_FULL + i), 1);
       mbar_init(bar(B::V_EMPTY + i), 1);
     }
+    mbar_init(bar(B::CS_FULL), 1);
+    mbar_init(bar(B::CS_EMPTY), kRopeThreads);
     mbar_init(bar(B::DONE), 1);
     ctl->abort = 0;
     fence_mbar_init();
@@ -537,6 +647,10 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
     tma_prefetch_desc(&p.tmk);
     tma_prefetch_desc(&p.tmv);
     if (p.krot) tma_prefetch_desc(&p.tmk_rot);
+    if (C::CS_BYTES) {
+      tma_prefetch_desc(&p.tmcos);
+      tma_prefetch_desc(&p.tmsin);
+    }
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(&ctl->tmem_base), C::TMEM_COLS);
@@ -556,11 +670,20 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
     regs_dec<REG_CTRL>();
     if (warp == 0 && lane == 0) {
       // ---------------------------------------------------------- TMA producer
-      uint32_t q_it[2] = {0, 0}, k_it = 0, v_it = 0;
+      uint32_t q_it[2] = {0, 0}, k_it = 0, v_it = 0, cs_it = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
         const Unit U = decode_unit(p, u, n_long);
         const int ns = U.has_b ? 2 : 1;
+        if constexpr (C::CS_BYTES != 0) {
+          ok = bounded_wait(bar(B::CS_EMPTY), (cs_it & 1) ^ 1, p, abort_flag,
+                            FRATTN_STATUS_WAIT_TIMEOUT | 0x03);
+          if (!ok) break;
+          mbar_arrive_expect_tx(bar(B::CS_FULL), C::CS_BYTES);
+          tma_load_2d(sbase + C::OFF_CS, &p.tmcos, bar(B::CS_FULL), 0, U.q0a);
+          tma_load_2d(sbase + C::OFF_CS + C::CS_BYTES / 2, &p.tmsin, bar(B::CS_FULL), 0, U.q0a);
+          ++cs_it;
+        }
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
           if (x >= ns || !ok) break;
@@ -645,9 +768,11 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t vaddr = sbase + C::OFF_V + (vi % ST) * C::TILE_BYTES;
+                const uint64_t vdesc = make_sdesc(vaddr, kBlkBytes, 256, SW32);
 #pragma unroll
                 for (int kk = 0; kk < kTileN / 16; ++kk) {
-                  const uint64_t bd = make_sdesc(vaddr + kk * 512, kBlkBytes, 256, SW32);
+                  // descriptor of the kk-th 16-row group: advance the start-address field
+                  const uint64_t bd = vdesc + static_cast<uint64_t>((kk * 512) >> 4);
                   umma_ts(tmem + C::TMEM_O + 128u * x, s_col + kk * 8, bd, IDESC_O,
                           (j > 1 || kk > 0) ? 1u : 0u);
                 }
@@ -663,10 +788,12 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
                 tc_fence_after();
                 const uint32_t qaddr = sbase + qbuf(x, qs[x]);
                 const uint32_t kaddr = sbase + C::OFF_K + (ki % ST) * C::TILE_BYTES;
+                const uint64_t qdesc = make_sdesc(qaddr, 16, 256, SW32);
+                const uint64_t kdesc = make_sdesc(kaddr, 16, 256, SW32);
 #pragma unroll
                 for (int kb = 0; kb < C::KB; ++kb) {
-                  const uint64_t ad = make_sdesc(qaddr + kb * kBlkBytes, 16, 256, SW32);
-                  const uint64_t bd = make_sdesc(kaddr + kb * kBlkBytes, 16, 256, SW32);
+                  const uint64_t ad = qdesc + static_cast<uint64_t>((kb * kBlkBytes) >> 4);
+                  const uint64_t bd = kdesc + static_cast<uint64_t>((kb * kBlkBytes) >> 4);
                   umma_ss(s_col, ad, bd, IDESC_S, kb > 0 ? 1u : 0u);
                 }
                 umma_commit(bar(B::S_FULL + x));
@@ -693,11 +820,18 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
     // ------------------------------------------------------------ RoPE warpgroup
     regs_dec<REG_ROPE>();
     const int r = threadIdx.x - 128;
-    uint32_t q_it[2] = {0, 0}, k_it = 0;
+    uint32_t q_it[2] = {0, 0}, k_it = 0, cs_it = 0;
     bool ok = true;
+    const uint8_t* cs_tile = C::CS_BYTES ? smem + C::OFF_CS : nullptr;
     for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
       const Unit U = decode_unit(p, u, n_long);
       const int ns = U.has_b ? 2 : 1;
+      if constexpr (C::CS_BYTES != 0) {
+        ok = bounded_wait(bar(B::CS_FULL), cs_it & 1, p, abort_flag,
+                          FRATTN_STATUS_WAIT_TIMEOUT | 0x22);
+        if (!ok) break;
+        ++cs_it;
+      }
 #pragma unroll
       for (int x = 0; x < 2; ++x) {
         if (x >= ns || !ok) break;
@@ -705,7 +839,9 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
         ok = bounded_wait(bar(B::Q_FULL + x * QB + qs), (q_it[x] / QB) & 1, p, abort_flag,
                           FRATTN_STATUS_WAIT_TIMEOUT | 0x20);
         if (!ok) break;
-        rope_tile<D, MODE, TI, TC>(smem + qbuf(x, qs), x ? U.q0b : U.q0a, p, r);
+        const int qrow = x ? U.q0b : U.q0a;
+        rope_tile<D, MODE, TI, TC>(smem + qbuf(x, qs), qrow, p, r,
+                                   qrow == U.q0a ? cs_tile : nullptr);
         fence_proxy_async_smem();
         mbar_arrive(bar(B::Q_READY + x * QB + qs));
         ++q_it[x];
@@ -720,13 +856,16 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
           ok = bounded_wait(bar(B::K_FULL + ks), (k_it / ST) & 1, p, abort_flag,
                             FRATTN_STATUS_WAIT_TIMEOUT | 0x21);
           if (!ok) break;
+          const int krow = U.kv0 + j * kTileN;
           if (!(U.shared && p.krot))  // long segments: K arrives pre-rotated
-            rope_tile<D, MODE, TI, TC>(smem + C::OFF_K + ks * C::TILE_BYTES, U.kv0 + j * kTileN, p, r);
+            rope_tile<D, MODE, TI, TC>(smem + C::OFF_K + ks * C::TILE_BYTES, krow, p, r,
+                                       krow == U.q0a ? cs_tile : nullptr);
           fence_proxy_async_smem();
           mbar_arrive(bar(B::K_READY + ks));
           ++k_it;
         }
       }
+      if (C::CS_BYTES != 0 && ok) mbar_arrive(bar(B::CS_EMPTY));
     }
   } else {
     // ------------------------------------------------------------ softmax WGs
@@ -738,6 +877,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
     const uint32_t o_addr = lane_addr + C::TMEM_O + 128u * x;
     const float sl2 = 1.4426950408889634f * rsqrtf(static_cast<float>(D));
     constexpr float kRescaleLog2 = 8.0f;  // move the reference max only when it grows by 2^8
+    constexpr int kPolyOf8 = FRATTN_POLY_OF_8;
     uint32_t s_it = 0, o_it = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
@@ -783,16 +923,15 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
           for (int i = 0; i < kTileN; ++i)
             if (i < lo_r || i >= hi_r) s[i] = -INFINITY;
         }
-        float mxp[8];
+        float mxq[4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) mxp[i] = fmaxf(s[i], s[i + 8]);
+        for (int q = 0; q < 4; ++q) mxq[q] = fmaxf(s[2 * q], s[2 * q + 1]);
 #pragma unroll
-        for (int i = 16; i < kTileN; i += 8) {
+        for (int i = 8; i < kTileN; i += 8) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e) mxp[e] = fmaxf(mxp[e], s[i + e]);
+          for (int q = 0; q < 4; ++q) mxq[q] = max3(mxq[q], s[i + 2 * q], s[i + 2 * q + 1]);
         }
-        const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                               fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+        const float mx = max3(fmaxf(mxq[0], mxq[1]), mxq[2], mxq[3]);
         // The exponent reference only moves when the running max grows by more
         // than 2^8 (or is still -inf); the final 1/l uses the same reference,
         // so the result is exact up to rounding.
@@ -804,23 +943,38 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
           m_ref = mx;
         }
         const float mb = (m_ref == -INFINITY ? 0.f : m_ref) * sl2;
-        // p = 2^(s*scale - ref), written as packed pairs over the first 64 TMEM
-        // columns of the S region (already consumed into registers), 32 at a time.
-        float sp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        // p = 2^(s*scale - ref): pairs in fp32x2; kPolyOf8 of every 8 pairs go
+        // through the FMA-pipe exp2, the rest through MUFU ex2. P is written as
+        // packed pairs over the first 64 TMEM columns of the S region (already
+        // consumed into registers), 32 columns at a time.
+        const uint64_t scale2 = f2pack(sl2, sl2);
+        const uint64_t bias2 = f2pack(-mb, -mb);
+        uint64_t sp2[4] = {0, 0, 0, 0};
 #pragma unroll
         for (int c = 0; c < kTileN / 32; ++c) {
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            const float p0 = ex2(fmaf(s[c * 32 + 2 * e], sl2, -mb));
-            const float p1 = ex2(fmaf(s[c * 32 + 2 * e + 1], sl2, -mb));
-            sp[(2 * e) & 7] += p0;
-            sp[(2 * e + 1) & 7] += p1;
+            const uint64_t xa = fma2(f2pack(s[c * 32 + 2 * e], s[c * 32 + 2 * e + 1]), scale2, bias2);
+            uint64_t pp;
+            if ((e & 7) < kPolyOf8) {
+              pp = exp2_poly2(xa);
+            } else {
+              float a0, a1;
+              f2unpack(xa, a0, a1);
+              pp = f2pack(ex2(a0), ex2(a1));
+            }
+            sp2[e & 3] = add2(sp2[e & 3], pp);
+            float p0, p1;
+            f2unpack(pp, p0, p1);
             pk[e] = pack2<TI>(p0, p1);
           }
           tmem_st16(s_addr + c * 16, pk);
         }
-        const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
+        float sa, sb, sc, sd;
+        f2unpack(add2(sp2[0], sp2[1]), sa, sb);
+        f2unpack(add2(sp2[2], sp2[3]), sc, sd);
+        const float sum = (sa + sb) + (sc + sd);
         l = l * alpha + sum;
         // O holds PV(j-1) complete: S_FULL(j) was committed after it.
         if (__any_sync(0xffffffffu, rescale)) {
@@ -848,11 +1002,13 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
       const bool store = lo < hi;
       const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
       TI* orow = static_cast<TI*>(p.out) + (static_cast<size_t>(row) * p.H + h) * D;
+      uint32_t oo[D / 16][16];
+#pragma unroll
+      for (int c = 0; c < D / 16; ++c) tmem_ld16(o_addr + c * 16, oo[c]);
+      tmem_ld_wait();
 #pragma unroll
       for (int c = 0; c < D / 16; ++c) {
-        uint32_t rr[16];
-        tmem_ld16(o_addr + c * 16, rr);
-        tmem_ld_wait();
+        const uint32_t (&rr)[16] = oo[c];
         if (store) {
           uint4 w0, w1;
           w0.x = pack2<TI>(__uint_as_float(rr[0]) * inv_l, __uint_as_float(rr[1]) * inv_l);
@@ -886,20 +1042,39 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
 constexpr int kPrepThreads = 1024;
 
 __device__ __forceinline__ int block_exclusive_scan(int v, int* tmp, int* total) {
-  // Simple Hillis-Steele scan over kPrepThreads values in shared memory.
-  const int t = threadIdx.x;
-  tmp[t] = v;
-  __syncthreads();
-  for (int off = 1; off < kPrepThreads; off <<= 1) {
-    const int x = t >= off ? tmp[t - off] : 0;
-    __syncthreads();
-    tmp[t] += x;
-    __syncthreads();
+  // Warp-shuffle scan, then a scan of the 32 warp totals by warp 0.
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  int x = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, off);
+    if (lane >= off) x += y;
   }
-  const int incl = tmp[t];
-  *total = tmp[kPrepThreads - 1];
+  if (lane == 31) tmp[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    int y = lane < kPrepThreads / 32 ? tmp[lane] : 0;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int z = __shfl_up_sync(0xffffffffu, y, off);
+      if (lane >= off) y += z;
+    }
+    tmp[32 + lane] = y;  // inclusive scan of warp totals
+  }
+  __syncthreads();
+  const int incl = x + (w > 0 ? tmp[32 + w - 1] : 0);
+  *total = tmp[32 + kPrepThreads / 32 - 1];
   __syncthreads();
   return incl - v;
+}
+
+// upper_bound over cu_seqlens held in shared or global memory (plain loads).
+__device__ __forceinline__ int upper_bound_any(const int32_t* cu, int lo, int hi, int x) {
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (cu[mid] > x) hi = mid; else lo = mid + 1;
+  }
+  return lo;
 }
 
 template <typename TI, int D>
@@ -907,8 +1082,15 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
     build_worklist(const int32_t* __restrict__ cu, int nseg, int T, int H, WorkItem* items,
                    int* header, TI* out, int32_t* status, float* pos_tab, int pos_rows,
                    float theta) {
-  __shared__ int tmp[kPrepThreads];
+  __shared__ int tmp[64];
+  constexpr int kCuSmem = 8192;  // cu_seqlens entries staged in shared memory
+  __shared__ int32_t s_cu[kCuSmem];
   const int tid = threadIdx.x;
+  const bool cu_in_smem = nseg + 1 <= kCuSmem;
+  if (cu_in_smem)
+    for (int i = tid; i <= nseg; i += kPrepThreads) s_cu[i] = cu[i];
+  __syncthreads();
+  const int32_t* cuv = cu_in_smem ? s_cu : cu;
 
   // Validate cu_seqlens: non-decreasing, inside [0, T].
   int bad = 0;
@@ -991,23 +1173,23 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
       int a = max(c * kTileM, c_first);
       int e = min(c * kTileM + kTileM, min(T, c_last));
       if (a < e) {
-        int sa = upper_bound_cu(cu, 0, nseg + 1, a) - 1;
-        if (cu[sa + 1] - cu[sa] > kTileM) {
-          a = cu[sa + 1];
-          if (a < e) sa = upper_bound_cu(cu, 0, nseg + 1, a) - 1;
+        int sa = upper_bound_any(cuv, 0, nseg + 1, a) - 1;
+        if (cuv[sa + 1] - cuv[sa] > kTileM) {
+          a = cuv[sa + 1];
+          if (a < e) sa = upper_bound_any(cuv, 0, nseg + 1, a) - 1;
         }
-        if (a < e && cu[sa + 1] - cu[sa] <= kTileM) {
-          int se = upper_bound_cu(cu, 0, nseg + 1, e - 1) - 1;
-          if (cu[se + 1] - cu[se] > kTileM) {
-            e = cu[se];
-            if (a < e) se = upper_bound_cu(cu, 0, nseg + 1, e - 1) - 1;
+        if (a < e && cuv[sa + 1] - cuv[sa] <= kTileM) {
+          int se = upper_bound_any(cuv, 0, nseg + 1, e - 1) - 1;
+          if (cuv[se + 1] - cuv[se] > kTileM) {
+            e = cuv[se];
+            if (a < e) se = upper_bound_any(cuv, 0, nseg + 1, e - 1) - 1;
           }
           if (a < e) {
             has = 1;
             w.q0 = a;
             w.q1 = e;
-            w.kv0 = cu[sa];
-            w.kv1 = cu[se + 1];
+            w.kv0 = cuv[sa];
+            w.kv1 = cuv[se + 1];
             w.seg_lo = sa;
             w.seg_hi = se;
             w.kind = kItemPacked;
@@ -1100,11 +1282,29 @@ int make_qkv_map(CUtensorMap* m, const void* base, int T, int H, int D, bool bf1
   return r == CUDA_SUCCESS ? 0 : FRATTN_E_TMAP;
 }
 
+// [T, D/2] cos or sin table; box {D/2, 128}, no swizzle.
+int make_cs_map(CUtensorMap* m, const void* base, int T, int D, int cs_dtype) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (!enc) return FRATTN_E_TMAP;
+  const int esz = cs_dtype == FRATTN_F32 ? 4 : 2;
+  const CUtensorMapDataType dt = cs_dtype == FRATTN_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : cs_dtype == FRATTN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(D / 2), static_cast<cuuint64_t>(T)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(D / 2) * esz};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(D / 2), static_cast<cuuint32_t>(kTileM)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : FRATTN_E_TMAP;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 template <int D, int MODE, typename TI, typename TC>
 int launch_attn(const Params& prm, cudaStream_t st) {
-  using C = Cfg<D>;
+  using C = Cfg<D, MODE == kRopeTable ? static_cast<int>(sizeof(TC)) : 0>;
   auto kern = fused_rope_attn_kernel<D, MODE, TI, TC>;
   // Per-device flag; setting the attribute twice is harmless, so races are benign.
   static unsigned long long attr_set = 0;
@@ -1246,6 +1446,9 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
     prm.krot = ws + krot_off;
     if (make_qkv_map(&prm.tmk_rot, prm.krot, T, H, D, bf16)) return FRATTN_E_TMAP;
   }
+  if (MODE == kRopeTable &&
+      (make_cs_map(&prm.tmcos, cos, T, D, cs_dtype) || make_cs_map(&prm.tmsin, sin, T, D, cs_dtype)))
+    return FRATTN_E_TMAP;
   prm.k = k;
   prm.cos = cos;
   prm.sin = sin;

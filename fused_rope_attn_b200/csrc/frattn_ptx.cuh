@@ -206,3 +206,15 @@ __device__ __forceinline__ void regs_dec() {
 }
 
 }  // namespace frattn
+
+namespace frattn {
+// 2-D tiled load (no multicast): coordinates innermost first.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* desc, uint32_t bar, int c0,
+                                            int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+}  // namespace frattn
