@@ -52,6 +52,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=100)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-encoder", action="store_true", help="skip the 32-layer encoder timing")
     return ap.parse_args()
 
 
@@ -248,6 +249,47 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------- encoder (config 4)
+def encoder_timing(torch, dev, reps=10):
+    """32-layer random-weight encoder on one 1344x1344 image (9216 tokens), fused vs unfused
+    attention, each forward replayed from a CUDA graph (device time, no host overhead)."""
+    from fused_rope_attn_b200.encoder import (EncoderConfig, VisionEncoder, encoder_flops, encoder_inputs,
+                                              rel_l2, unfused_backend)
+    grid = [(1, 96, 96)]
+    cfg = EncoderConfig()
+    enc = VisionEncoder(cfg, device=dev, dtype=torch.bfloat16)
+    x = encoder_inputs(grid, cfg.hidden, seed=0, device=dev)
+    plan = enc.plan(grid)
+    res, outs = {}, {}
+    s = torch.cuda.Stream(device=dev)
+    for attn in ("fused", "unfused"):
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                enc(x, grid, attn=attn, plan=plan)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            y = enc(x, grid, attn=attn, plan=plan)
+        for _ in range(2):
+            g.replay()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize(dev)
+        res[attn] = a.elapsed_time(b) / reps
+        outs[attn] = y.clone()
+        del g
+    fl = encoder_flops(grid, cfg)
+    return {"image": "1344x1344 (9216 tokens, 144 windows + 1 full segment)", "layers": cfg.depth,
+            "fused_ms": res["fused"], "unfused_ms": res["unfused"], "speedup": res["unfused"] / res["fused"],
+            "unfused_arm": "RoPE in bf16 (torch elementwise) + " + unfused_backend(),
+            "gemm_tflop": fl["gemm"] / 1e12, "attention_tflop": fl["attention"] / 1e12,
+            "fused_vs_unfused_rel_l2": rel_l2(outs["fused"], outs["unfused"]), "launch": "CUDA graph replay"}
+
+
 # --------------------------------------------------------------------------- GPU
 def run_ours(args):
     import torch
@@ -397,6 +439,11 @@ def run_ours(args):
             "clocks": clk,
             "device_status": status,
         }
+        if not args.no_encoder:
+            try:
+                line["encoder"] = encoder_timing(torch, dev)
+            except Exception as exc:  # noqa: BLE001 - report, do not lose the main line
+                line["encoder"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
         if not args.no_cpu_baseline:
             v, cores, sample = cpu_baseline(budget_s=10.0)
             line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
