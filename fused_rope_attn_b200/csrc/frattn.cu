@@ -429,47 +429,6 @@ __device__ __forceinline__ void rope_tile(uint8_t* tile, int row0, const Params&
   rope_batches<D, MODE, TI, TC, 0, BS>(tile, row0, p, r0, cs_smem);
 }
 
-// Rotate row r of up to four 128 x D tiles that cover the same tokens (the Q
-// and K tiles of both slots of a window unit), reading each cos/sin chunk from
-// shared memory once for all of them.
-template <int D, typename TI, typename TC>
-__device__ __forceinline__ void rope_tiles_shared_rows(uint8_t* t0, uint8_t* t1, uint8_t* t2, uint8_t* t3,
-                                                       int nt, const uint8_t* cs_smem, int row, int T, int r) {
-  constexpr int NP = D / 16;
-  if (row >= T) return;  // rows past the end hold TMA zeros
-  const TC* cst = reinterpret_cast<const TC*>(cs_smem) + r * (D / 2);
-#pragma unroll
-  for (int c = 0; c < NP; ++c) {
-    float cs[8], sn[8];
-    load8_smem<TC>(cst + c * 8, cs);
-    load8_smem<TC>(cst + kTileM * (D / 2) + c * 8, sn);
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      if (t >= nt) break;
-      uint8_t* tile = t == 0 ? t0 : (t == 1 ? t1 : (t == 2 ? t2 : t3));
-      uint4* pa = reinterpret_cast<uint4*>(tile + chunk_off(r, c));
-      uint4* pb = reinterpret_cast<uint4*>(tile + chunk_off(r, c + NP));
-      float x0[8], x1[8];
-      unpack8<TI>(*pa, x0);
-      unpack8<TI>(*pb, x1);
-      uint4 oa, ob;
-      uint32_t* wa = reinterpret_cast<uint32_t*>(&oa);
-      uint32_t* wb = reinterpret_cast<uint32_t*>(&ob);
-#pragma unroll
-      for (int e = 0; e < 8; e += 2) {
-        const float a0 = x0[e] * cs[e] - x1[e] * sn[e];
-        const float a1 = x0[e + 1] * cs[e + 1] - x1[e + 1] * sn[e + 1];
-        const float b0 = x0[e] * sn[e] + x1[e] * cs[e];
-        const float b1 = x0[e + 1] * sn[e + 1] + x1[e + 1] * cs[e + 1];
-        wa[e / 2] = pack2<TI>(a0, a1);
-        wb[e / 2] = pack2<TI>(b0, b1);
-      }
-      *pa = oa;
-      *pb = ob;
-    }
-  }
-}
-
 __device__ __forceinline__ int upper_bound_cu(const int32_t* cu, int lo, int hi, int x) {
   // first index i in [lo, hi) with cu[i] > x (hi if none)
   while (lo < hi) {
@@ -872,39 +831,6 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
                           FRATTN_STATUS_WAIT_TIMEOUT | 0x22);
         if (!ok) break;
         ++cs_it;
-      }
-      const int nkv0 = (U.kv1 - U.kv0 + kTileN - 1) / kTileN;
-      if (C::CS_BYTES != 0 && ST >= 2 && !U.shared && nkv0 == 1 && U.kv0 == U.q0a) {
-        // Window unit: Q_A, Q_B, K_A, K_B cover the same tokens -> one pass.
-        const int qs0 = q_it[0] % QB, qs1 = q_it[1] % QB;
-        const uint32_t k0 = k_it, k1 = k_it + 1;
-        ok = bounded_wait(bar(B::Q_FULL + qs0), (q_it[0] / QB) & 1, p, abort_flag,
-                          FRATTN_STATUS_WAIT_TIMEOUT | 0x20);
-        if (ok && ns > 1)
-          ok = bounded_wait(bar(B::Q_FULL + QB + qs1), (q_it[1] / QB) & 1, p, abort_flag,
-                            FRATTN_STATUS_WAIT_TIMEOUT | 0x20);
-        if (ok)
-          ok = bounded_wait(bar(B::K_FULL + k0 % ST), (k0 / ST) & 1, p, abort_flag,
-                            FRATTN_STATUS_WAIT_TIMEOUT | 0x21);
-        if (ok && ns > 1)
-          ok = bounded_wait(bar(B::K_FULL + k1 % ST), (k1 / ST) & 1, p, abort_flag,
-                            FRATTN_STATUS_WAIT_TIMEOUT | 0x21);
-        if (!ok) break;
-        rope_tiles_shared_rows<D, TI, TC>(smem + qbuf(0, qs0), smem + C::OFF_K + (k0 % ST) * C::TILE_BYTES,
-                                          smem + qbuf(1, qs1), smem + C::OFF_K + (k1 % ST) * C::TILE_BYTES,
-                                          2 * ns, cs_tile, U.q0a + r, p.T, r);
-        fence_proxy_async_smem();
-        mbar_arrive(bar(B::Q_READY + qs0));
-        mbar_arrive(bar(B::K_READY + k0 % ST));
-        ++q_it[0];
-        if (ns > 1) {
-          mbar_arrive(bar(B::Q_READY + QB + qs1));
-          mbar_arrive(bar(B::K_READY + k1 % ST));
-          ++q_it[1];
-        }
-        k_it += ns;
-        mbar_arrive(bar(B::CS_EMPTY));
-        continue;
       }
 #pragma unroll
       for (int x = 0; x < 2; ++x) {
