@@ -448,6 +448,8 @@ __device__ __forceinline__ int upper_bound_cu(const int32_t* cu, int lo, int hi,
 template <int D, int MODE, typename TI, typename TC>
 __global__ void __launch_bounds__(256) rotate_k_long(const __grid_constant__ Params p) {
   constexpr int NP = D / 16;
+  griddep_wait();               // work list of this call is complete
+  griddep_launch_dependents();  // let the attention kernel start its prologue
   const int n_long = __ldg(p.header + 1);
   const TI* kin = static_cast<const TI*>(p.k);
   TI* kout = static_cast<TI*>(p.krot);
@@ -661,6 +663,9 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
 
+  // Everything above overlaps the previous kernel of this call (programmatic
+  // dependent launch); the work list and rotated K are read only after this.
+  griddep_wait();
   const int n_items = __ldg(p.header);
   const int n_long = __ldg(p.header + 1);
   const int n_units = n_long * p.H + (n_items - n_long) * ((p.H + 1) >> 1);
@@ -1082,6 +1087,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
     build_worklist(const int32_t* __restrict__ cu, int nseg, int T, int H, WorkItem* items,
                    int* header, TI* out, int32_t* status, float* pos_tab, int pos_rows,
                    float theta) {
+  griddep_launch_dependents();  // dependents only start prologues; they wait for completion
   __shared__ int tmp[64];
   constexpr int kCuSmem = 8192;  // cu_seqlens entries staged in shared memory
   __shared__ int32_t s_cu[kCuSmem];
@@ -1318,11 +1324,23 @@ int launch_attn(const Params& prm, cudaStream_t st) {
     attr_set |= bit;
   }
   const int grid = sm_count_for_current_device();
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t lc = {};
+  lc.stream = st;
+  lc.attrs = &attr;
+  lc.numAttrs = 1;
   if (prm.krot) {
-    rotate_k_long<D, MODE, TI, TC><<<2 * grid, 256, 0, st>>>(prm);
-    if (cudaGetLastError() != cudaSuccess) return FRATTN_E_CUDA;
+    lc.gridDim = dim3(2 * grid);
+    lc.blockDim = dim3(256);
+    lc.dynamicSmemBytes = 0;
+    if (cudaLaunchKernelEx(&lc, rotate_k_long<D, MODE, TI, TC>, prm) != cudaSuccess) return FRATTN_E_CUDA;
   }
-  kern<<<grid, kThreads, C::SMEM_BYTES, st>>>(prm);
+  lc.gridDim = dim3(grid);
+  lc.blockDim = dim3(kThreads);
+  lc.dynamicSmemBytes = C::SMEM_BYTES;
+  if (cudaLaunchKernelEx(&lc, kern, prm) != cudaSuccess) return FRATTN_E_CUDA;
   return cudaGetLastError() == cudaSuccess ? 0 : FRATTN_E_CUDA;
 }
 

@@ -218,3 +218,13 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* desc, uint
       : "memory");
 }
 }  // namespace frattn
+
+namespace frattn {
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialization attribute may start while its predecessor runs; it must
+// execute griddep_wait() before touching the predecessor's results.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+}  // namespace frattn
