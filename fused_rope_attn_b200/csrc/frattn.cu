@@ -453,25 +453,29 @@ __global__ void __launch_bounds__(256) rotate_k_long(const __grid_constant__ Par
   const int n_long = __ldg(p.header + 1);
   const TI* kin = static_cast<const TI*>(p.k);
   TI* kout = static_cast<TI*>(p.krot);
-  // One flat index space over all long items (each covers at most 256 rows).
-  const int per_item = 2 * kTileM * p.H * NP;
+  // One thread per (row, head) of the long items (each covers at most 256 rows):
+  // the whole 2*D-byte K row and its cos/sin row are loaded before any math.
+  const int per_item = 2 * kTileM * p.H;
   const long long total = static_cast<long long>(n_long) * per_item;
   for (long long e = blockIdx.x * blockDim.x + threadIdx.x; e < total;
        e += static_cast<long long>(gridDim.x) * blockDim.x) {
-    {
-      const int i = static_cast<int>(e / per_item);
-      const int rem = static_cast<int>(e % per_item);
-      const int c = rem % NP;
-      const int rh = rem / NP;
-      const int h = rh % p.H;
-      const int row = __ldg(&p.items[i].q0) + rh / p.H;
-      if (row >= __ldg(&p.items[i].q1)) continue;
-      const size_t base = (static_cast<size_t>(row) * p.H + h) * D;
-      const uint4 ua = __ldg(reinterpret_cast<const uint4*>(kin + base + 8 * c));
-      const uint4 ub = __ldg(reinterpret_cast<const uint4*>(kin + base + D / 2 + 8 * c));
+    const int i = static_cast<int>(e / per_item);
+    const int rem = static_cast<int>(e % per_item);
+    const int h = rem % p.H;
+    const int row = __ldg(&p.items[i].q0) + rem / p.H;
+    if (row >= __ldg(&p.items[i].q1)) continue;
+    const size_t base = (static_cast<size_t>(row) * p.H + h) * D;
+    uint4 ua[NP], ub[NP];
+#pragma unroll
+    for (int c = 0; c < NP; ++c) {
+      ua[c] = __ldg(reinterpret_cast<const uint4*>(kin + base + 8 * c));
+      ub[c] = __ldg(reinterpret_cast<const uint4*>(kin + base + D / 2 + 8 * c));
+    }
+#pragma unroll
+    for (int c = 0; c < NP; ++c) {
       float x0[8], x1[8], cs[8], sn[8];
-      unpack8<TI>(ua, x0);
-      unpack8<TI>(ub, x1);
+      unpack8<TI>(ua[c], x0);
+      unpack8<TI>(ub[c], x1);
       rope_coeffs<D, MODE, TC>(p, row, 8 * c, cs, sn);
       uint4 oa, ob;
       uint32_t* wa = reinterpret_cast<uint32_t*>(&oa);
