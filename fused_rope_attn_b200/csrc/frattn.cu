@@ -213,6 +213,13 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
 }
 
 template <typename T>
+__device__ __forceinline__ T from_f32(float x);
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+
+template <typename T>
 __device__ __forceinline__ float to_f32(T x);
 template <>
 __device__ __forceinline__ float to_f32<float>(float x) { return x; }
@@ -421,12 +428,62 @@ __device__ __forceinline__ void rope_batches(uint8_t* tile, int row0, const Para
   }
 }
 
+// cos/sin of rotary index i for token `row` (scalar; used when D/2 is not a
+// multiple of 8, e.g. D = 72).
+template <int D, int MODE, typename TC>
+__device__ __forceinline__ void rope_coeff1(const Params& p, int row, int i, const TC* cs_row, float& c,
+                                            float& s) {
+  if (MODE == kRopeTable && cs_row != nullptr) {
+    c = to_f32<TC>(cs_row[i]);
+    s = to_f32<TC>(cs_row[kTileM * (D / 2) + i]);
+  } else if constexpr (MODE == kRopeTable) {
+    c = to_f32<TC>(__ldg(static_cast<const TC*>(p.cos) + static_cast<size_t>(row) * (D / 2) + i));
+    s = to_f32<TC>(__ldg(static_cast<const TC*>(p.sin) + static_cast<size_t>(row) * (D / 2) + i));
+  } else {
+    constexpr int Q4 = D / 4;
+    const int2 hw = __ldg(reinterpret_cast<const int2*>(p.pos_hw) + row);
+    const int pos = i < Q4 ? hw.x : hw.y;
+    const size_t idx = static_cast<size_t>(pos) * Q4 + (i < Q4 ? i : i - Q4);
+    c = __ldg(p.pos_tab + idx);
+    s = __ldg(p.pos_tab + static_cast<size_t>(p.pos_rows) * Q4 + idx);
+  }
+}
+
+// Element-wise rotation of row r (pairs j, j + D/2 that straddle 8-element
+// chunks), for head dims with D/2 not a multiple of 8.
+template <int D, int MODE, typename TI, typename TC>
+__device__ __forceinline__ void rope_row_elementwise(uint8_t* tile, int row0, const Params& p, int r,
+                                                     const uint8_t* cs_smem) {
+  const int row = row0 + r;
+  if (row >= p.T) return;
+  const TC* cs_row = cs_smem ? reinterpret_cast<const TC*>(cs_smem) + r * (D / 2) : nullptr;
+  auto at = [&](int e) -> TI* {
+    return reinterpret_cast<TI*>(tile + chunk_off(r, e >> 3) + (e & 7) * 2);
+  };
+#pragma unroll 4
+  for (int j = 0; j < D / 2; ++j) {
+    TI* pa = at(j);
+    TI* pb = at(j + D / 2);
+    const float x0 = to_f32<TI>(*pa), x1 = to_f32<TI>(*pb);
+    float c, sn;
+    rope_coeff1<D, MODE, TC>(p, row, j, cs_row, c, sn);
+    const float a = x0 * c - x1 * sn;
+    const float b = x0 * sn + x1 * c;
+    *pa = from_f32<TI>(a);
+    *pb = from_f32<TI>(b);
+  }
+}
+
 // Rotate the rows of a raw 128 x D tile owned by this rope thread.
 template <int D, int MODE, typename TI, typename TC>
 __device__ __forceinline__ void rope_tile(uint8_t* tile, int row0, const Params& p, int r0,
                                           const uint8_t* cs_smem = nullptr) {
-  constexpr int BS = 1;  // one chunk pair per batch: the rope warpgroup runs on 64 registers
-  rope_batches<D, MODE, TI, TC, 0, BS>(tile, row0, p, r0, cs_smem);
+  if constexpr (D % 16 == 0) {
+    constexpr int BS = 1;  // one chunk pair per batch: the rope warpgroup runs on 64 registers
+    rope_batches<D, MODE, TI, TC, 0, BS>(tile, row0, p, r0, cs_smem);
+  } else {
+    rope_row_elementwise<D, MODE, TI, TC>(tile, row0, p, r0, cs_smem);
+  }
 }
 
 __device__ __forceinline__ int upper_bound_cu(const int32_t* cu, int lo, int hi, int x) {
@@ -465,6 +522,16 @@ __global__ void __launch_bounds__(256) rotate_k_long(const __grid_constant__ Par
     const int row = __ldg(&p.items[i].q0) + rem / p.H;
     if (row >= __ldg(&p.items[i].q1)) continue;
     const size_t base = (static_cast<size_t>(row) * p.H + h) * D;
+    if constexpr (D % 16 != 0) {
+      for (int j = 0; j < D / 2; ++j) {
+        const float x0 = to_f32<TI>(kin[base + j]), x1 = to_f32<TI>(kin[base + D / 2 + j]);
+        float c, sn;
+        rope_coeff1<D, MODE, TC>(p, row, j, static_cast<const TC*>(nullptr), c, sn);
+        kout[base + j] = from_f32<TI>(x0 * c - x1 * sn);
+        kout[base + D / 2 + j] = from_f32<TI>(x0 * sn + x1 * c);
+      }
+      continue;
+    }
     uint4 ua[NP], ub[NP];
 #pragma unroll
     for (int c = 0; c < NP; ++c) {
@@ -545,11 +612,13 @@ __device__ __forceinline__ Unit decode_unit(const Params& p, int u, int n_long) 
 
 template <int D, int CSB>
 struct Cfg {
-  static_assert(D % 16 == 0 && D >= 32 && D <= 128, "D must be a multiple of 16 in [32,128]");
-  static constexpr int KB = D / 16;                  // 32-byte column blocks per row
-  static constexpr int TILE_BYTES = kTileM * D * 2;  // one 128 x D tile
+  static_assert(D % 8 == 0 && D >= 32 && D <= 128, "D must be a multiple of 8 in [32,128]");
+  static constexpr int DP = (D + 15) / 16 * 16;      // tile width: D rounded up to the MMA K step
+  static constexpr int KB = DP / 16;                 // 32-byte column blocks per row
+  static constexpr int TILE_BYTES = kTileM * DP * 2; // one 128 x DP tile (TMA zero-fills D..DP)
   // cos/sin rows of the current unit staged in smem (table mode): [128][D/2] x 2
-  static constexpr int CS_BYTES = 2 * kTileM * (D / 2) * CSB;
+  // (only when a cos/sin row is a whole number of 16-byte units, as TMA requires)
+  static constexpr int CS_BYTES = ((D / 2) * CSB) % 16 == 0 ? 2 * kTileM * (D / 2) * CSB : 0;
   static constexpr int BAR_BYTES = 512;
   static constexpr int kBudget = 232448 - BAR_BYTES - 1024;
   static constexpr bool fits(int qb, int st) {
@@ -606,7 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
   using B = Bars<ST, QB>;
   constexpr bool kBF16 = std::is_same<TI, __nv_bfloat16>::value;
   constexpr uint32_t IDESC_S = make_idesc_f16(kBF16, kTileM, kTileN, false);
-  constexpr uint32_t IDESC_O = make_idesc_f16(kBF16, kTileM, D, true);
+  constexpr uint32_t IDESC_O = make_idesc_f16(kBF16, kTileM, C::DP, true);
   constexpr uint32_t SW32 = 6;
   static_assert(B::COUNT * 8 + 16 <= C::BAR_BYTES, "barrier area");
 
@@ -988,7 +1057,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
         // O holds PV(j-1) complete: S_FULL(j) was committed after it.
         if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
-          for (int c = 0; c < D / 16; ++c) {
+          for (int c = 0; c < C::DP / 16; ++c) {
             uint32_t rr[16];
             tmem_ld16(o_addr + c * 16, rr);
             tmem_ld_wait();
@@ -1011,12 +1080,12 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
       const bool store = lo < hi;
       const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
       TI* orow = static_cast<TI*>(p.out) + (static_cast<size_t>(row) * p.H + h) * D;
-      uint32_t oo[D / 16][16];
+      uint32_t oo[C::DP / 16][16];
 #pragma unroll
-      for (int c = 0; c < D / 16; ++c) tmem_ld16(o_addr + c * 16, oo[c]);
+      for (int c = 0; c < C::DP / 16; ++c) tmem_ld16(o_addr + c * 16, oo[c]);
       tmem_ld_wait();
 #pragma unroll
-      for (int c = 0; c < D / 16; ++c) {
+      for (int c = 0; c < C::DP / 16; ++c) {
         const uint32_t (&rr)[16] = oo[c];
         if (store) {
           uint4 w0, w1;
@@ -1028,8 +1097,8 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
           w1.y = pack2<TI>(__uint_as_float(rr[10]) * inv_l, __uint_as_float(rr[11]) * inv_l);
           w1.z = pack2<TI>(__uint_as_float(rr[12]) * inv_l, __uint_as_float(rr[13]) * inv_l);
           w1.w = pack2<TI>(__uint_as_float(rr[14]) * inv_l, __uint_as_float(rr[15]) * inv_l);
-          reinterpret_cast<uint4*>(orow + c * 16)[0] = w0;
-          reinterpret_cast<uint4*>(orow + c * 16)[1] = w1;
+          if (c * 16 < D) reinterpret_cast<uint4*>(orow + c * 16)[0] = w0;
+          if (c * 16 + 8 < D) reinterpret_cast<uint4*>(orow + c * 16)[1] = w1;
         }
       }
       tc_fence_before();
@@ -1370,6 +1439,7 @@ template <int MODE>
 int dispatch_d(const Params& prm, int D, int in_dtype, int cs_dtype, cudaStream_t st) {
   switch (D) {
     case 64: return dispatch_in<64, MODE>(prm, in_dtype, cs_dtype, st);
+    case 72: return dispatch_in<72, MODE>(prm, in_dtype, cs_dtype, st);
     case 80: return dispatch_in<80, MODE>(prm, in_dtype, cs_dtype, st);
     case 96: return dispatch_in<96, MODE>(prm, in_dtype, cs_dtype, st);
     case 128: return dispatch_in<128, MODE>(prm, in_dtype, cs_dtype, st);
@@ -1389,6 +1459,7 @@ int launch_prep_t(const int32_t* cu, int nseg, int T, int H, int D, WorkItem* it
                                                        pos_rows, theta);                        \
     break;
     FRATTN_PREP_CASE(64)
+    FRATTN_PREP_CASE(72)
     FRATTN_PREP_CASE(80)
     FRATTN_PREP_CASE(96)
     FRATTN_PREP_CASE(128)
@@ -1406,7 +1477,7 @@ int common_checks(const void* q, const void* k, const void* v, const int32_t* cu
                   int H, int D, int in_dtype, void* out, void* ws) {
   if (!q || !k || !v || !cu || !out || !ws) return FRATTN_E_NULL;
   if (T < 0 || H <= 0 || nseg < 1) return FRATTN_E_SHAPE;
-  if (D != 64 && D != 80 && D != 96 && D != 128) return FRATTN_E_SHAPE;
+  if (D != 64 && D != 72 && D != 80 && D != 96 && D != 128) return FRATTN_E_SHAPE;
   if (in_dtype != FRATTN_BF16 && in_dtype != FRATTN_F16) return FRATTN_E_DTYPE;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !aligned16(ws))
     return FRATTN_E_ALIGN;
@@ -1468,7 +1539,10 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
     prm.krot = ws + krot_off;
     if (make_qkv_map(&prm.tmk_rot, prm.krot, T, H, D, bf16)) return FRATTN_E_TMAP;
   }
-  if (MODE == kRopeTable &&
+  // cos/sin rows are staged through TMA only when a row is a multiple of 16 bytes
+  // (the kernel's Cfg::CS_BYTES makes the same decision).
+  const int cs_esz = cs_dtype == FRATTN_F32 ? 4 : 2;
+  if (MODE == kRopeTable && ((D / 2) * cs_esz) % 16 == 0 &&
       (make_cs_map(&prm.tmcos, cos, T, D, cs_dtype) || make_cs_map(&prm.tmsin, sin, T, D, cs_dtype)))
     return FRATTN_E_TMAP;
   prm.k = k;

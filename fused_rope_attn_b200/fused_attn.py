@@ -36,7 +36,7 @@ __all__ = [
     "SUPPORTED_HEAD_DIMS",
 ]
 
-SUPPORTED_HEAD_DIMS = (64, 80, 96, 128)
+SUPPORTED_HEAD_DIMS = (64, 72, 80, 96, 128)
 
 _DT = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
 

@@ -96,6 +96,7 @@ KERNEL_CASES = [
     ("full16x16_f16", [(1, 16, 16)], False, 2, torch.float16, 80),
     ("win8x24_f32", [(1, 8, 24)], True, 2, torch.float32, 80),
     ("multi_f16", [(1, 8, 8), (1, 6, 10)], True, 1, torch.float16, 64),
+    ("hd72_win16x12_f16", [(1, 16, 12)], True, 2, torch.float16, 72),  # the reference bench.py:31-34 head dim
 ]
 
 

@@ -50,7 +50,7 @@ def _fwd(lib, **kw):
 def test_argument_validation_before_launch():
     lib = _lib.load()
     assert _fwd(lib, q=None) == _lib.E_NULL
-    assert _fwd(lib, D=72) == _lib.E_SHAPE
+    assert _fwd(lib, D=72 + 2) == _lib.E_SHAPE
     assert _fwd(lib, H=0) == _lib.E_SHAPE
     assert _fwd(lib, nseg=0) == _lib.E_SHAPE
     assert _fwd(lib, dt=_lib.F32) == _lib.E_DTYPE

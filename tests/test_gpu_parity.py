@@ -64,7 +64,7 @@ def test_dtypes(dtype, cs_dtype):
     assert_close(run(*case), oracle(*case))
 
 
-@pytest.mark.parametrize("D", [64, 80, 96, 128])
+@pytest.mark.parametrize("D", [64, 72, 80, 96, 128])
 def test_head_dims(D):
     case = cu_case([0, 64, 128, 390, 400], H=2, D=D, seed=D)
     assert_close(run(*case), oracle(*case))
@@ -112,6 +112,15 @@ def test_noncontiguous_and_int64_cpu_cu():
     out = fused_rope_attention(qt.to(DEV), k.to(DEV), v.to(DEV), cos.to(DEV), sin.to(DEV), cu.to(torch.int64))
     torch.cuda.synchronize()
     assert_close(out, oracle(q, k, v, cos, sin, cu))
+
+
+@pytest.mark.parametrize("cs_dtype", [torch.float32, torch.bfloat16])
+def test_head_dim_72_fp16_reference_bench_shape(cs_dtype):
+    """The reference's own benchmark configuration: fp16, head_dim 72 (bench.py:31-34)."""
+    case = grid_case([(1, 32, 32)], True, H=16, D=72, dtype=torch.float16, cs_dtype=cs_dtype, seed=72)
+    assert_close(run(*case), oracle(*case))
+    case = grid_case([(1, 32, 32)], False, H=4, D=72, dtype=torch.float16, cs_dtype=cs_dtype, seed=73)
+    assert_close(run(*case), oracle(*case))
 
 
 def test_wrapper_value_errors():
