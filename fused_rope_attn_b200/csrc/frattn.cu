@@ -347,85 +347,36 @@ __device__ __forceinline__ void rope_coeffs(const Params& p, int row, int i0, fl
   }
 }
 
-// Rotate row r of a raw 128 x D tile in shared memory in place (rotate-half
-// RoPE, fp32 math, one rounding to the element type, fused_attn.py:340-345).
-// All shared and global loads of the row are issued before any arithmetic so
-// their latencies overlap.
-// Rotate chunks [C0, C1) of NR tile rows (r0 + i * kRopeThreads) in place.
-// All shared and global loads of the batch are issued before any arithmetic so
-// that their latencies overlap (rotate-half RoPE in fp32, one rounding to the
-// element type, fused_attn.py:340-345).
-template <int D, int MODE, typename TI, typename TC, int NR, int C0, int C1>
-__device__ __forceinline__ void rope_rows_part(uint8_t* tile, int row0, const Params& p, int r0,
-                                               const uint8_t* cs_smem) {
-  constexpr int NP = D / 16;  // pairs of 8-element chunks: chunk c <-> chunk c + NP
-  constexpr int N = C1 - C0;
-  uint4 xa[NR][N], xb[NR][N];
-  float cs[NR][N][8], sn[NR][N][8];
-#pragma unroll
-  for (int i = 0; i < NR; ++i) {
-    const int r = r0 + i * kRopeThreads;
-#pragma unroll
-    for (int c = 0; c < N; ++c) {
-      xa[i][c] = *reinterpret_cast<const uint4*>(tile + chunk_off(r, C0 + c));
-      xb[i][c] = *reinterpret_cast<const uint4*>(tile + chunk_off(r, C0 + c + NP));
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < NR; ++i) {
-    const int row = min(row0 + r0 + i * kRopeThreads, p.T - 1);  // rows >= T hold TMA zeros
-    if (MODE == kRopeTable && cs_smem != nullptr) {
-      // cos/sin rows of this tile staged in shared memory: [128][D/2] cos, then sin
-      const TC* cst = reinterpret_cast<const TC*>(cs_smem) + (r0 + i * kRopeThreads) * (D / 2);
-#pragma unroll
-      for (int c = 0; c < N; ++c) {
-        load8_smem<TC>(cst + (C0 + c) * 8, cs[i][c]);
-        load8_smem<TC>(cst + kTileM * (D / 2) + (C0 + c) * 8, sn[i][c]);
-      }
-    } else {
-#pragma unroll
-      for (int c = 0; c < N; ++c) rope_coeffs<D, MODE, TC>(p, row, (C0 + c) * 8, cs[i][c], sn[i][c]);
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < NR; ++i) {
-    const int r = r0 + i * kRopeThreads;
-#pragma unroll
-    for (int c = 0; c < N; ++c) {
-      float x0[8], x1[8];
-      unpack8<TI>(xa[i][c], x0);
-      unpack8<TI>(xb[i][c], x1);
-      uint4 oa, ob;
-      uint32_t* wa = reinterpret_cast<uint32_t*>(&oa);
-      uint32_t* wb = reinterpret_cast<uint32_t*>(&ob);
-#pragma unroll
-      for (int e = 0; e < 8; e += 2) {
-        const float a0 = x0[e] * cs[i][c][e] - x1[e] * sn[i][c][e];
-        const float a1 = x0[e + 1] * cs[i][c][e + 1] - x1[e + 1] * sn[i][c][e + 1];
-        const float b0 = x0[e] * sn[i][c][e] + x1[e] * cs[i][c][e];
-        const float b1 = x0[e + 1] * sn[i][c][e + 1] + x1[e + 1] * cs[i][c][e + 1];
-        wa[e / 2] = pack2<TI>(a0, a1);
-        wb[e / 2] = pack2<TI>(b0, b1);
-      }
-      *reinterpret_cast<uint4*>(tile + chunk_off(r, C0 + c)) = oa;
-      *reinterpret_cast<uint4*>(tile + chunk_off(r, C0 + c + NP)) = ob;
-    }
-  }
-}
-
-// Rotate chunks [C0, NP) of the rows owned by this rope thread in batches of
-// BS chunks (table mode: 3 then 2 for D = 80; position mode gathers 16 table
-// values per chunk, so it works in smaller batches to stay inside its registers).
-template <int D, int MODE, typename TI, typename TC, int C0, int BS>
-__device__ __forceinline__ void rope_batches(uint8_t* tile, int row0, const Params& p, int r0,
-                                             const uint8_t* cs_smem) {
+// Rotate chunk pair (c, c + D/16) of row r of a 128 x D tile in place
+// (rotate-half RoPE in fp32, one rounding to the element type,
+// fused_attn.py:340-345). cos/sin come from the staged rows when given.
+template <int D, int MODE, typename TI, typename TC>
+__device__ __forceinline__ void rope_pair(uint8_t* tile, int row0, const Params& p, int r,
+                                          const uint8_t* cs_smem, int c) {
   constexpr int NP = D / 16;
-  constexpr int NR = kTileM / kRopeThreads;
-  if constexpr (C0 < NP) {
-    constexpr int C1 = (C0 + BS < NP) ? C0 + BS : NP;
-    rope_rows_part<D, MODE, TI, TC, NR, C0, C1>(tile, row0, p, r0, cs_smem);
-    rope_batches<D, MODE, TI, TC, C1, BS>(tile, row0, p, r0, cs_smem);
+  const uint4 ua = *reinterpret_cast<const uint4*>(tile + chunk_off(r, c));
+  const uint4 ub = *reinterpret_cast<const uint4*>(tile + chunk_off(r, c + NP));
+  float cs[8], sn[8];
+  if (MODE == kRopeTable && cs_smem != nullptr) {
+    const TC* cst = reinterpret_cast<const TC*>(cs_smem) + r * (D / 2) + c * 8;
+    load8_smem<TC>(cst, cs);
+    load8_smem<TC>(cst + kTileM * (D / 2), sn);
+  } else {
+    rope_coeffs<D, MODE, TC>(p, min(row0 + r, p.T - 1), c * 8, cs, sn);  // rows >= T hold TMA zeros
   }
+  float x0[8], x1[8];
+  unpack8<TI>(ua, x0);
+  unpack8<TI>(ub, x1);
+  uint4 oa, ob;
+  uint32_t* wa = reinterpret_cast<uint32_t*>(&oa);
+  uint32_t* wb = reinterpret_cast<uint32_t*>(&ob);
+#pragma unroll
+  for (int e = 0; e < 8; e += 2) {
+    wa[e / 2] = pack2<TI>(x0[e] * cs[e] - x1[e] * sn[e], x0[e + 1] * cs[e + 1] - x1[e + 1] * sn[e + 1]);
+    wb[e / 2] = pack2<TI>(x0[e] * sn[e] + x1[e] * cs[e], x0[e + 1] * sn[e + 1] + x1[e + 1] * cs[e + 1]);
+  }
+  *reinterpret_cast<uint4*>(tile + chunk_off(r, c)) = oa;
+  *reinterpret_cast<uint4*>(tile + chunk_off(r, c + NP)) = ob;
 }
 
 // cos/sin of rotary index i for token `row` (scalar; used when D/2 is not a
@@ -479,8 +430,12 @@ template <int D, int MODE, typename TI, typename TC>
 __device__ __forceinline__ void rope_tile(uint8_t* tile, int row0, const Params& p, int r0,
                                           const uint8_t* cs_smem = nullptr) {
   if constexpr (D % 16 == 0) {
-    constexpr int BS = 1;  // one chunk pair per batch: the rope warpgroup runs on 64 registers
-    rope_batches<D, MODE, TI, TC, 0, BS>(tile, row0, p, r0, cs_smem);
+    // One chunk pair per iteration, as a real loop: the rotation shares the
+    // SM's instruction caches with the softmax code, and the unrolled form
+    // (D/16 copies at each call site) measured slower in the window regime.
+    constexpr int NP = D / 16;
+#pragma unroll 1
+    for (int c = 0; c < NP; ++c) rope_pair<D, MODE, TI, TC>(tile, row0, p, r0, cs_smem, c);
   } else {
     rope_row_elementwise<D, MODE, TI, TC>(tile, row0, p, r0, cs_smem);
   }
@@ -501,7 +456,7 @@ __device__ __forceinline__ int upper_bound_cu(const int32_t* cu, int lo, int hi,
 // the attention kernel) turns L/128 rotations of each K tile into one, at the
 // cost of reading K and writing the rotated copy once (HBM-bound, a few us).
 // Short segments keep the fully fused path (their K tiles are used once).
-// Same arithmetic as rope_rows_part: fp32 rotation, one rounding.
+// Same arithmetic as rope_pair: fp32 rotation, one rounding.
 template <int D, int MODE, typename TI, typename TC>
 __global__ void __launch_bounds__(256) rotate_k_long(const __grid_constant__ Params p) {
   constexpr int NP = D / 16;
