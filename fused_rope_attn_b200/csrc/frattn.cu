@@ -1129,9 +1129,9 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
   // Validate cu_seqlens: non-decreasing, inside [0, T].
   int bad = 0;
   for (int s = tid; s <= nseg; s += kPrepThreads) {
-    const int a = cu[s];
+    const int a = cuv[s];
     if (a < 0 || a > T) bad = 1;
-    if (s < nseg && cu[s + 1] < a) bad = 1;
+    if (s < nseg && cuv[s + 1] < a) bad = 1;
   }
   bad = __syncthreads_or(bad);
   if (bad) {
@@ -1158,7 +1158,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
     }
   }
 
-  const int c_first = cu[0], c_last = cu[nseg];
+  const int c_first = cuv[0], c_last = cuv[nseg];
   // Zero rows not covered by any segment.
   {
     const size_t row_elems = static_cast<size_t>(H) * D;  // multiple of 8
@@ -1177,8 +1177,8 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
     const int s = s0 + tid;
     int a = 0, b = 0, n = 0;
     if (s < nseg) {
-      a = cu[s];
-      b = cu[s + 1];
+      a = cuv[s];
+      b = cuv[s + 1];
       if (b - a > kTileM) n = (b - a + 2 * kTileM - 1) / (2 * kTileM);
     }
     const int off = block_exclusive_scan(n, tmp, &total);
