@@ -1444,7 +1444,8 @@ template <int MODE>
 int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const void* sin,
              int cs_dtype, const int32_t* pos_hw, int max_position, float theta,
              const int32_t* cu, int nseg, int T, int H, int D, int in_dtype, void* out,
-             void* workspace, size_t ws_bytes, int32_t* status, void* stream) {
+             void* workspace, size_t ws_bytes, int32_t* status, void* stream,
+             int max_seqlen = 0) {
   int rc = common_checks(q, k, v, cu, nseg, T, H, D, in_dtype, out, workspace);
   if (rc) return rc;
   size_t need = 0;
@@ -1487,10 +1488,15 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
   if (make_qkv_map(&prm.tmq, q, T, H, D, bf16) || make_qkv_map(&prm.tmk, k, T, H, D, bf16) ||
       make_qkv_map(&prm.tmv, v, T, H, D, bf16))
     return FRATTN_E_TMAP;
-  // Rotated-K buffer after the work list (and table) when the workspace has room.
+  // Rotated-K buffer after the work list (and table) when the workspace has
+  // room. A caller's max_seqlen <= one tile says no segment is long, so the
+  // pre-rotation pass would find nothing to do and is not launched. The hint
+  // only selects that path: long segments are still correct without it
+  // (their K tiles are then rotated inside the attention kernel).
   const size_t krot_off = (need + 255) & ~size_t(255);
   const size_t krot_bytes = static_cast<size_t>(T) * H * D * 2;
-  if (ws_bytes >= krot_off + krot_bytes) {
+  const bool no_long = max_seqlen > 0 && max_seqlen <= kTileM;
+  if (ws_bytes >= krot_off + krot_bytes && !no_long) {
     prm.krot = ws + krot_off;
     if (make_qkv_map(&prm.tmk_rot, prm.krot, T, H, D, bf16)) return FRATTN_E_TMAP;
   }
@@ -1599,19 +1605,18 @@ int frattn_fwd(const void* q, const void* k, const void* v, const void* cos, con
                int cs_dtype, const int32_t* cu_seqlens, int nseg, int T, int H, int D,
                int max_seqlen, int in_dtype, void* out, void* workspace, size_t workspace_bytes,
                int32_t* status, void* stream) {
-  (void)max_seqlen;
   return fwd_impl<kRopeTable>(q, k, v, cos, sin, cs_dtype, nullptr, 0, 0.f, cu_seqlens, nseg, T,
-                              H, D, in_dtype, out, workspace, workspace_bytes, status, stream);
+                              H, D, in_dtype, out, workspace, workspace_bytes, status, stream,
+                              max_seqlen);
 }
 
 int frattn_fwd_pos(const void* q, const void* k, const void* v, const int32_t* pos_hw,
                    int max_position, float theta, const int32_t* cu_seqlens, int nseg, int T,
                    int H, int D, int max_seqlen, int in_dtype, void* out, void* workspace,
                    size_t workspace_bytes, int32_t* status, void* stream) {
-  (void)max_seqlen;
   return fwd_impl<kRopePos>(q, k, v, nullptr, nullptr, FRATTN_F32, pos_hw, max_position, theta,
                             cu_seqlens, nseg, T, H, D, in_dtype, out, workspace, workspace_bytes,
-                            status, stream);
+                            status, stream, max_seqlen);
 }
 
 int frattn_selftest_wait_timeout(int32_t* status, uint64_t limit_ns, void* stream) {

@@ -11,9 +11,11 @@ Mirrors the public interface of the reference module ``fused_attn.py``
 
 Additions that keep the call a drop-in:
 
-* keyword ``max_seqlen`` is accepted and ignored: the on-device scheduler derives the
-  work list from ``cu_seqlens`` itself, so no ``.item()`` host sync is needed
-  (the reference syncs at fused_attn.py:211);
+* keyword ``max_seqlen`` is an optional hint, never required: the on-device
+  scheduler derives the work list from ``cu_seqlens`` itself, so no ``.item()``
+  host sync is needed (the reference syncs at fused_attn.py:211). A hint of at
+  most 128 (window layers) skips the K pre-rotation pass and its workspace;
+  results are the same with or without it;
 * ``fused_rope_attention_pos`` takes integer (h, w) patch positions instead of
   materialised cos/sin tables and evaluates the rotary angles in the kernel.
 """
@@ -265,7 +267,9 @@ def fused_rope_attention(
     cu = _check_cu(cu_seqlens, q.device)
     nseg = cu.numel() - 1
     lib = _lib.load()
-    ws_bytes = _lib.workspace_bytes(total, nseg) + _lib.workspace_bytes_rotated_k(total, heads, hd)
+    ws_bytes = _lib.workspace_bytes(total, nseg)
+    if not (max_seqlen and 0 < max_seqlen <= 128):
+        ws_bytes += _lib.workspace_bytes_rotated_k(total, heads, hd)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
@@ -313,8 +317,9 @@ def fused_rope_attention_pos(
     cu = _check_cu(cu_seqlens, q.device)
     nseg = cu.numel() - 1
     lib = _lib.load()
-    ws_bytes = (_lib.workspace_bytes_pos(total, nseg, max_position, hd)
-                + _lib.workspace_bytes_rotated_k(total, heads, hd))
+    ws_bytes = _lib.workspace_bytes_pos(total, nseg, max_position, hd)
+    if not (max_seqlen and 0 < max_seqlen <= 128):
+        ws_bytes += _lib.workspace_bytes_rotated_k(total, heads, hd)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream

@@ -87,7 +87,8 @@ int frattn_workspace_bytes_rotated_k(int total_tokens, int num_heads, int head_d
  *   q, k, v, out : [T, H, D] contiguous, element type in_dtype (F16 or BF16)
  *   cos, sin     : [T, D/2] contiguous, element type cs_dtype (F32, F16, BF16)
  *   cu_seqlens   : [nseg + 1] int32, non-decreasing, values in [0, T]
- *   max_seqlen   : optional hint (<= 0: unknown); the kernel never needs it
+ *   max_seqlen   : optional hint (<= 0: unknown). A value <= 128 skips the K
+ *                  pre-rotation pass (no segment is long); results do not depend on it
  *   workspace    : >= frattn_workspace_bytes(T, nseg) bytes of device memory
  *   status       : device int32 (may be NULL); set non-zero on a device error
  *   stream       : cudaStream_t the kernels are launched on

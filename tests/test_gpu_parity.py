@@ -178,6 +178,23 @@ def test_position_entry_point_matches_tables():
     assert (out_pos.float() - out_tab.float()).abs().max().item() <= 2e-2
 
 
+@pytest.mark.parametrize("windowed", [True, False])
+def test_max_seqlen_hint_changes_nothing(windowed):
+    # The hint only decides whether long segments' K is pre-rotated in a
+    # separate pass; a true, a missing and a wrong (too small) hint give the
+    # same result (the K rotation is the same fp32 arithmetic on either path), and
+    # all of them match the oracle.
+    case = grid_case([(1, 32, 48)], windowed, H=4, seed=7)
+    true_max = int((case[5][1:] - case[5][:-1]).max())
+    want = oracle(*case)
+    ref = run(*case)
+    assert_close(ref, want)
+    for hint in (true_max, 64, 1):
+        out = run(*case, max_seqlen=hint)
+        assert_close(out, want)
+        assert (out.float() - ref.float()).abs().max().item() <= 1e-2
+
+
 def test_deterministic():
     case = grid_case([(1, 32, 32)], False, H=4, seed=4)
     a = run(*case)
