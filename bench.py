@@ -372,6 +372,16 @@ def run_ours(args):
     elapsed_ms = e_start.elapsed_time(e_end)
     per_var = {var: statistics.mean(a.elapsed_time(b) for a, b in ev[var]) for var in variants}
     status = last_status(dev)
+    # The timed outputs come from graph replays: check them against eager calls.
+    graph_err = 0.0
+    for i in range(R):
+        for var in variants:
+            t_ = sets[i][var]
+            with torch.cuda.stream(stream):
+                graphs[i][var].replay()
+            torch.cuda.synchronize()
+            ref = fused_rope_attention(t_["q"], t_["k"], t_["v"], t_["cos"], t_["sin"], t_["cu"])
+            graph_err = max(graph_err, (t_["out"].float() - ref.float()).abs().max().item())
     if world > 1:
         t = torch.tensor([elapsed_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -436,6 +446,7 @@ def run_ours(args):
             # work list + attention per call, + the K pre-rotation when a segment is long
             "gpu_launches": K * sum(2 + (hint[var] > 128) for var in variants),
             "layer_us": {var: per_var[var] * 1e3 for var in variants},
+            "graph_vs_eager_max_abs": graph_err,
             "roofline": {"bound": "tensor", "kernel": "full-attention call (4096-token segment)",
                          "achieved": ach_tf, "peak": tflops, "unit": "TFLOP/s", "frac": ach_tf / tflops,
                          "peak_source": f"{src} bf16 burst", "traffic": traffic.get("full")},

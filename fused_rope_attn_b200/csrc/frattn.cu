@@ -81,6 +81,20 @@ struct __align__(16) WorkItem {
   int kind, pad;
 };
 
+// The work list, its header and the position table are written by
+// build_worklist in the same call. The kernels that read them start early
+// (programmatic dependent launch) and may be resident before those writes, so
+// they read them through L2 (ld.global.cg), never through the non-coherent
+// read-only path, which may keep lines from before the writes.
+__device__ __forceinline__ WorkItem load_item(const WorkItem* it) {
+  const int4 a = __ldcg(reinterpret_cast<const int4*>(it));
+  const int4 b = __ldcg(reinterpret_cast<const int4*>(it) + 1);
+  WorkItem w;
+  w.q0 = a.x; w.q1 = a.y; w.kv0 = a.z; w.kv1 = a.w;
+  w.seg_lo = b.x; w.seg_hi = b.y; w.kind = b.z; w.pad = b.w;
+  return w;
+}
+
 constexpr int kHeaderBytes = 128;
 __host__ __device__ inline size_t max_items(int T) {
   const size_t chunks = (static_cast<size_t>(T) + kTileM - 1) / kTileM;
@@ -341,8 +355,8 @@ __device__ __forceinline__ void rope_coeffs(const Params& p, int row, int i0, fl
       const int pos = i < Q4 ? hw.x : hw.y;
       const int j = i < Q4 ? i : i - Q4;
       const size_t idx = static_cast<size_t>(pos) * Q4 + j;
-      cs[e] = __ldg(ct + idx);
-      sn[e] = __ldg(st + idx);
+      cs[e] = __ldcg(ct + idx);
+      sn[e] = __ldcg(st + idx);
     }
   }
 }
@@ -395,8 +409,8 @@ __device__ __forceinline__ void rope_coeff1(const Params& p, int row, int i, con
     const int2 hw = __ldg(reinterpret_cast<const int2*>(p.pos_hw) + row);
     const int pos = i < Q4 ? hw.x : hw.y;
     const size_t idx = static_cast<size_t>(pos) * Q4 + (i < Q4 ? i : i - Q4);
-    c = __ldg(p.pos_tab + idx);
-    s = __ldg(p.pos_tab + static_cast<size_t>(p.pos_rows) * Q4 + idx);
+    c = __ldcg(p.pos_tab + idx);
+    s = __ldcg(p.pos_tab + static_cast<size_t>(p.pos_rows) * Q4 + idx);
   }
 }
 
@@ -462,7 +476,7 @@ __global__ void __launch_bounds__(256) rotate_k_long(const __grid_constant__ Par
   constexpr int NP = D / 16;
   griddep_wait();               // work list of this call is complete
   griddep_launch_dependents();  // let the attention kernel start its prologue
-  const int n_long = __ldg(p.header + 1);
+  const int n_long = __ldcg(p.header + 1);
   const TI* kin = static_cast<const TI*>(p.k);
   TI* kout = static_cast<TI*>(p.krot);
   // One thread per (row, head) of the long items (each covers at most 256 rows):
@@ -474,8 +488,8 @@ __global__ void __launch_bounds__(256) rotate_k_long(const __grid_constant__ Par
     const int i = static_cast<int>(e / per_item);
     const int rem = static_cast<int>(e % per_item);
     const int h = rem % p.H;
-    const int row = __ldg(&p.items[i].q0) + rem / p.H;
-    if (row >= __ldg(&p.items[i].q1)) continue;
+    const int row = __ldcg(&p.items[i].q0) + rem / p.H;
+    if (row >= __ldcg(&p.items[i].q1)) continue;
     const size_t base = (static_cast<size_t>(row) * p.H + h) * D;
     if constexpr (D % 16 != 0) {
       for (int j = 0; j < D / 2; ++j) {
@@ -537,7 +551,7 @@ __device__ __forceinline__ Unit decode_unit(const Params& p, int u, int n_long) 
   const int hp = (p.H + 1) >> 1;
   WorkItem it;
   if (u < n_long * p.H) {
-    it = p.items[u / p.H];
+    it = load_item(p.items + u / p.H);
     const int h = u % p.H;
     U.q0a = it.q0;
     U.q1a = min(it.q0 + kTileM, it.q1);
@@ -548,7 +562,7 @@ __device__ __forceinline__ Unit decode_unit(const Params& p, int u, int n_long) 
     U.shared = true;
   } else {
     const int v = u - n_long * p.H;
-    it = p.items[n_long + v / hp];
+    it = load_item(p.items + n_long + v / hp);
     const int g = v % hp;
     U.q0a = U.q0b = it.q0;
     U.q1a = U.q1b = it.q1;
@@ -694,8 +708,8 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
   // Everything above overlaps the previous kernel of this call (programmatic
   // dependent launch); the work list and rotated K are read only after this.
   griddep_wait();
-  const int n_items = __ldg(p.header);
-  const int n_long = __ldg(p.header + 1);
+  const int n_items = __ldcg(p.header);
+  const int n_long = __ldcg(p.header + 1);
   const int n_units = n_long * p.H + (n_items - n_long) * ((p.H + 1) >> 1);
   const int wg = warp >> 2;
 

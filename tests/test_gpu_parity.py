@@ -215,3 +215,28 @@ def test_reference_kernel_golden_vectors():
         ref = K[f"{name}/out"].astype(np.float32)
         err = np.abs(out - ref)
         assert err.max() <= MAX_ABS and err.mean() <= MEAN_ABS, (name, err.max(), err.mean())
+
+
+@pytest.mark.parametrize("windowed", [True, False])
+@pytest.mark.parametrize("hint", [None, "true"])
+def test_cuda_graph_replay_matches_eager(windowed, hint):
+    # Replayed from a CUDA graph, the call's kernels launch back to back with
+    # programmatic dependent launch; the attention kernel then starts before
+    # the work list is written and must still read the finished list.
+    case = grid_case([(1, 48, 48)], windowed, H=8, seed=11)
+    q, k, v, cos, sin, cu = (t.to(DEV) for t in case)
+    ms = int((cu[1:] - cu[:-1]).max()) if hint else None
+    eager = fused_rope_attention(q, k, v, cos, sin, cu, max_seqlen=ms)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        fused_rope_attention(q, k, v, cos, sin, cu, max_seqlen=ms)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        out = fused_rope_attention(q, k, v, cos, sin, cu, max_seqlen=ms)
+    for _ in range(3):
+        g.replay()
+        torch.cuda.synchronize()
+        assert last_status() == 0
+        assert (out.float() - eager.float()).abs().max().item() <= 1e-2
+    assert_close(out, oracle(*case))
