@@ -1083,10 +1083,10 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
 }
 
 // ------------------------------------------------------------------ scheduler
-// One CTA of 1024 threads builds the work list from cu_seqlens (see the file
+// One CTA of 256 threads builds the work list from cu_seqlens (see the file
 // header). Long items come first (largest kv ranges first per segment order),
 // packed items after them.
-constexpr int kPrepThreads = 1024;
+constexpr int kPrepThreads = 256;
 
 __device__ __forceinline__ int block_exclusive_scan(int v, int* tmp, int* total) {
   // Warp-shuffle scan, then a scan of the 32 warp totals by warp 0.
