@@ -455,6 +455,43 @@ __device__ __forceinline__ void rope_tile(uint8_t* tile, int row0, const Params&
   }
 }
 
+// Rotate row r of a raw 128 x D Q tile (shared memory) into TMEM lane r at
+// column qcol: element e of the rotated row goes to column qcol + e / 2 as a
+// packed pair, the A-operand layout of a TMEM-sourced MMA. The smem tile is
+// only read. Warp-converged (tcgen05.st is .sync.aligned).
+template <int D, int MODE, typename TI, typename TC>
+__device__ __forceinline__ void rope_q_to_tmem(const uint8_t* tile, int row0, const Params& p, int r,
+                                               const uint8_t* cs_smem, uint32_t qcol) {
+  static_assert(D % 16 == 0, "whole 8-element chunks");
+  constexpr int NP = D / 16;
+#pragma unroll 1
+  for (int c = 0; c < NP; ++c) {
+    const uint4 ua = *reinterpret_cast<const uint4*>(tile + chunk_off(r, c));
+    const uint4 ub = *reinterpret_cast<const uint4*>(tile + chunk_off(r, c + NP));
+    float cs[8], sn[8];
+    if (MODE == kRopeTable && cs_smem != nullptr) {
+      const TC* cst = reinterpret_cast<const TC*>(cs_smem) + r * (D / 2) + c * 8;
+      load8_smem<TC>(cst, cs);
+      load8_smem<TC>(cst + kTileM * (D / 2), sn);
+    } else {
+      rope_coeffs<D, MODE, TC>(p, min(row0 + r, p.T - 1), c * 8, cs, sn);
+    }
+    float x0[8], x1[8];
+    unpack8<TI>(ua, x0);
+    unpack8<TI>(ub, x1);
+    uint4 oa, ob;
+    uint32_t* wa = reinterpret_cast<uint32_t*>(&oa);
+    uint32_t* wb = reinterpret_cast<uint32_t*>(&ob);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      wa[e / 2] = pack2<TI>(x0[e] * cs[e] - x1[e] * sn[e], x0[e + 1] * cs[e + 1] - x1[e + 1] * sn[e + 1]);
+      wb[e / 2] = pack2<TI>(x0[e] * sn[e] + x1[e] * cs[e], x0[e + 1] * sn[e + 1] + x1[e + 1] * cs[e + 1]);
+    }
+    tmem_st4(qcol + 4 * c, oa);
+    tmem_st4(qcol + 4 * (c + NP), ob);
+  }
+}
+
 __device__ __forceinline__ int upper_bound_cu(const int32_t* cu, int lo, int hi, int x) {
   // first index i in [lo, hi) with cu[i] > x (hi if none)
   while (lo < hi) {
@@ -606,6 +643,11 @@ struct Cfg {
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t TMEM_S = 0;
   static constexpr uint32_t TMEM_O = 256;
+  // Rotated Q of slot X lives in TMEM behind O_X (columns DP .. DP + DP/2 of
+  // the 128-column O region) when it fits; S then takes its A operand from
+  // TMEM and the rotation never writes shared memory.
+  static constexpr bool Q_TMEM = (D % 16 == 0) && (DP + DP / 2 <= 128);
+  static constexpr uint32_t TMEM_Q = TMEM_O + DP;
 };
 
 template <int ST, int QB>
@@ -839,9 +881,13 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
                 const uint64_t kdesc = make_sdesc(kaddr, 16, 256, SW32);
 #pragma unroll
                 for (int kb = 0; kb < C::KB; ++kb) {
-                  const uint64_t ad = qdesc + static_cast<uint64_t>((kb * kBlkBytes) >> 4);
                   const uint64_t bd = kdesc + static_cast<uint64_t>((kb * kBlkBytes) >> 4);
-                  umma_ss(s_col, ad, bd, IDESC_S, kb > 0 ? 1u : 0u);
+                  if constexpr (C::Q_TMEM) {
+                    umma_ts(s_col, tmem + C::TMEM_Q + 128u * x + kb * 8, bd, IDESC_S, kb > 0 ? 1u : 0u);
+                  } else {
+                    const uint64_t ad = qdesc + static_cast<uint64_t>((kb * kBlkBytes) >> 4);
+                    umma_ss(s_col, ad, bd, IDESC_S, kb > 0 ? 1u : 0u);
+                  }
                 }
                 umma_commit(bar(B::S_FULL + x));
                 if (!U.shared || x == ns - 1) umma_commit(bar(B::K_EMPTY + ki % ST));
@@ -870,6 +916,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
     uint32_t q_it[2] = {0, 0}, k_it = 0, cs_it = 0;
     bool ok = true;
     const uint8_t* cs_tile = C::CS_BYTES ? smem + C::OFF_CS : nullptr;
+    const uint32_t q_lane = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);  // TMEM lane of row r
     for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
       const Unit U = decode_unit(p, u, n_long);
       const int ns = U.has_b ? 2 : 1;
@@ -883,13 +930,31 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
       for (int x = 0; x < 2; ++x) {
         if (x >= ns || !ok) break;
         const int qs = q_it[x] % QB;
-        ok = bounded_wait(bar(B::Q_FULL + x * QB + qs), (q_it[x] / QB) & 1, p, abort_flag,
-                          FRATTN_STATUS_WAIT_TIMEOUT | 0x20);
+        // warp-uniform result: the TMEM stores below are .sync.aligned
+        ok = bounded_wait_warp(bar(B::Q_FULL + x * QB + qs), (q_it[x] / QB) & 1, p, abort_flag,
+                               FRATTN_STATUS_WAIT_TIMEOUT | 0x20);
         if (!ok) break;
         const int qrow = x ? U.q0b : U.q0a;
-        rope_tile<D, MODE, TI, TC>(smem + qbuf(x, qs), qrow, p, r,
-                                   qrow == U.q0a ? cs_tile : nullptr);
-        fence_proxy_async_smem();
+        if constexpr (C::Q_TMEM) {
+          // The slot's Q columns are free once the previous Q of this slot is
+          // no longer read: its last S MMA committed Q_EMPTY.
+          if (q_it[x] > 0) {
+            const uint32_t pq = q_it[x] - 1;
+            ok = bounded_wait_warp(bar(B::Q_EMPTY + x * QB + pq % QB), (pq / QB) & 1, p,
+                                   abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x23);
+            if (!ok) break;
+          }
+          tc_fence_after();
+          rope_q_to_tmem<D, MODE, TI, TC>(smem + qbuf(x, qs), qrow, p, r,
+                                          qrow == U.q0a ? cs_tile : nullptr,
+                                          q_lane + C::TMEM_Q + 128u * x);
+          tmem_st_wait();
+          tc_fence_before();
+        } else {
+          rope_tile<D, MODE, TI, TC>(smem + qbuf(x, qs), qrow, p, r,
+                                     qrow == U.q0a ? cs_tile : nullptr);
+          fence_proxy_async_smem();
+        }
         mbar_arrive(bar(B::Q_READY + x * QB + qs));
         ++q_it[x];
       }
