@@ -666,7 +666,8 @@ struct Bars {
   static constexpr int CS_FULL = O_FULL + 2;          // cos/sin of the unit staged
   static constexpr int CS_EMPTY = CS_FULL + 1;         // ... and no longer needed
   static constexpr int DONE = CS_EMPTY + 1;
-  static constexpr int COUNT = DONE + 1;
+  static constexpr int QT_FREE = DONE + 1;            // [2] Q columns of slot X in TMEM reusable
+  static constexpr int COUNT = QT_FREE + 2;
 };
 
 // Register split (setmaxnreg): 128 x (REG_CTRL + REG_ROPE) + 256 x REG_SOFTMAX
@@ -708,9 +709,12 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
       for (int b = 0; b < QB; ++b) {
         mbar_init(bar(B::Q_FULL + x * QB + b), 1);
         mbar_init(bar(B::Q_READY + x * QB + b), kRopeThreads);
-        mbar_init(bar(B::Q_EMPTY + x * QB + b), 1);
+        // Q in TMEM: the rope warpgroup releases the smem buffer once it has
+        // read it; otherwise the last S MMA of the unit does.
+        mbar_init(bar(B::Q_EMPTY + x * QB + b), C::Q_TMEM ? kRopeThreads : 1);
       }
       mbar_init(bar(B::S_FULL + x), 1);
+      mbar_init(bar(B::QT_FREE + x), 1);
       mbar_init(bar(B::P_FULL + x), kSoftmaxThreads);
       mbar_init(bar(B::O_FULL + x), 1);
     }
@@ -891,7 +895,8 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
                 }
                 umma_commit(bar(B::S_FULL + x));
                 if (!U.shared || x == ns - 1) umma_commit(bar(B::K_EMPTY + ki % ST));
-                if (j == nkv - 1) umma_commit(bar(B::Q_EMPTY + x * QB + qs[x]));
+                if (j == nkv - 1)
+                  umma_commit(bar(C::Q_TMEM ? B::QT_FREE + x : B::Q_EMPTY + x * QB + qs[x]));
                 vprev[x] = v_it + (U.shared ? 0 : x);
               }
             }
@@ -937,17 +942,17 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
         const int qrow = x ? U.q0b : U.q0a;
         if constexpr (C::Q_TMEM) {
           // The slot's Q columns are free once the previous Q of this slot is
-          // no longer read: its last S MMA committed Q_EMPTY.
+          // no longer read: its last S MMA committed QT_FREE.
           if (q_it[x] > 0) {
-            const uint32_t pq = q_it[x] - 1;
-            ok = bounded_wait_warp(bar(B::Q_EMPTY + x * QB + pq % QB), (pq / QB) & 1, p,
-                                   abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x23);
+            ok = bounded_wait_warp(bar(B::QT_FREE + x), (q_it[x] - 1) & 1, p, abort_flag,
+                                   FRATTN_STATUS_WAIT_TIMEOUT | 0x23);
             if (!ok) break;
           }
           tc_fence_after();
           rope_q_to_tmem<D, MODE, TI, TC>(smem + qbuf(x, qs), qrow, p, r,
                                           qrow == U.q0a ? cs_tile : nullptr,
                                           q_lane + C::TMEM_Q + 128u * x);
+          mbar_arrive(bar(B::Q_EMPTY + x * QB + qs));  // smem tile read: reusable
           tmem_st_wait();
           tc_fence_before();
         } else {
