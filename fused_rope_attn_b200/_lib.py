@@ -21,6 +21,7 @@ NOALLOC_MAX_TOKENS = 65536
 E_CUDA, E_TMAP = 1, 2
 STATUS_WAIT_TIMEOUT = 0x100
 STATUS_BAD_SEQLENS = 0x200
+STATUS_BAD_POSITIONS = 0x400
 
 # Every symbol include/frattn.h declares, with (restype, argtypes).
 _vp, _i, _sz, _u64, _f = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_float

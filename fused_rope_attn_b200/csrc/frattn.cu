@@ -1197,8 +1197,8 @@ __device__ __forceinline__ int upper_bound_any(const int32_t* cu, int lo, int hi
 template <typename TI, int D>
 __global__ void __launch_bounds__(kPrepThreads, 1)
     build_worklist(const int32_t* __restrict__ cu, int nseg, int T, int H, WorkItem* items,
-                   int* header, TI* out, int32_t* status, float* pos_tab, int pos_rows,
-                   float theta) {
+                   int* header, TI* out, int32_t* status, const int32_t* pos_hw,
+                   float* pos_tab, int pos_rows, float theta) {
   griddep_launch_dependents();  // dependents only start prologues; they wait for completion
   __shared__ int tmp[64];
   constexpr int kCuSmem = 8192;  // cu_seqlens entries staged in shared memory
@@ -1218,11 +1218,21 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
     if (s < nseg && cuv[s + 1] < a) bad = 1;
   }
   bad = __syncthreads_or(bad);
-  if (bad) {
+  // (h, w) positions index a table of pos_rows rows: every one must be inside it.
+  int bad_pos = 0;
+  if (pos_hw != nullptr && !bad)
+    for (int e = tid; e < 2 * T; e += kPrepThreads) {
+      const int v = pos_hw[e];
+      if (v < 0 || v >= pos_rows) bad_pos = 1;
+    }
+  bad_pos = __syncthreads_or(bad_pos);
+  if (bad || bad_pos) {
     if (tid == 0) {
       header[0] = 0;
       header[1] = 0;
-      if (status) atomicCAS(reinterpret_cast<int*>(status), 0, FRATTN_STATUS_BAD_SEQLENS);
+      if (status)
+        atomicCAS(reinterpret_cast<int*>(status), 0,
+                  bad ? FRATTN_STATUS_BAD_SEQLENS : FRATTN_STATUS_BAD_POSITIONS);
     }
     return;
   }
@@ -1488,14 +1498,14 @@ int dispatch_d(const Params& prm, int D, int in_dtype, int cs_dtype, cudaStream_
 
 template <typename TI>
 int launch_prep_t(const int32_t* cu, int nseg, int T, int H, int D, WorkItem* items, int* header,
-                  void* out, int32_t* status, float* pos_tab, int pos_rows, float theta,
-                  cudaStream_t st) {
+                  void* out, int32_t* status, const int32_t* pos_hw, float* pos_tab, int pos_rows,
+                  float theta, cudaStream_t st) {
   switch (D) {
 #define FRATTN_PREP_CASE(DD)                                                                    \
   case DD:                                                                                      \
     build_worklist<TI, DD><<<1, kPrepThreads, 0, st>>>(cu, nseg, T, H, items, header,           \
-                                                       static_cast<TI*>(out), status, pos_tab,  \
-                                                       pos_rows, theta);                        \
+                                                       static_cast<TI*>(out), status, pos_hw,   \
+                                                       pos_tab, pos_rows, theta);               \
     break;
     FRATTN_PREP_CASE(64)
     FRATTN_PREP_CASE(72)
@@ -1558,10 +1568,10 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
     pos_tab = reinterpret_cast<float*>(ws + base);
   }
   if (in_dtype == FRATTN_BF16)
-    rc = launch_prep_t<__nv_bfloat16>(cu, nseg, T, H, D, items, header, out, status, pos_tab,
-                                      max_position, theta, st);
+    rc = launch_prep_t<__nv_bfloat16>(cu, nseg, T, H, D, items, header, out, status, pos_hw,
+                                      pos_tab, max_position, theta, st);
   else
-    rc = launch_prep_t<__half>(cu, nseg, T, H, D, items, header, out, status, pos_tab,
+    rc = launch_prep_t<__half>(cu, nseg, T, H, D, items, header, out, status, pos_hw, pos_tab,
                                max_position, theta, st);
   if (rc) return rc;
   if (T == 0) return 0;
@@ -1653,6 +1663,7 @@ const char* frattn_error_string(int code) {
     case FRATTN_E_NOALLOC_LIMIT:
       return "total_tokens exceeds FRATTN_NOALLOC_MAX_TOKENS for frattn_fwd_noalloc";
     case FRATTN_STATUS_BAD_SEQLENS: return "cu_seqlens is not non-decreasing within [0, T]";
+    case FRATTN_STATUS_BAD_POSITIONS: return "a pos_hw value is outside [0, max_position)";
     default:
       if ((code & 0xF00) == FRATTN_STATUS_WAIT_TIMEOUT) return "device wait timed out";
       return "unknown error";
@@ -1714,7 +1725,8 @@ int frattn_fwd_noalloc(const void* q, const void* k, const void* v, const void* 
                        int H, int D, int max_seqlen, int in_dtype, void* out, int32_t* status,
                        void* stream) {
   (void)max_seqlen;
-  if (T < 0 || T > FRATTN_NOALLOC_MAX_TOKENS) return FRATTN_E_NOALLOC_LIMIT;
+  if (T < 0) return FRATTN_E_SHAPE;
+  if (T > FRATTN_NOALLOC_MAX_TOKENS) return FRATTN_E_NOALLOC_LIMIT;
   size_t need = 0;
   int rc = frattn_workspace_bytes(T, nseg, &need);
   if (rc) return rc;
@@ -1723,10 +1735,11 @@ int frattn_fwd_noalloc(const void* q, const void* k, const void* v, const void* 
   rc = noalloc_scratch(&ws);
   if (rc) return rc;
   // The scheduler kernel rewrites the header and every item it uses on each
-  // call, so nothing in the array has to be cleared first.
+  // call, so nothing in the array has to be cleared first. Only the work-list
+  // bytes are handed over (never room for a rotated-K copy): every rotation
+  // stays inside the attention kernel.
   return fwd_impl<kRopeTable>(q, k, v, cos, sin, cs_dtype, nullptr, 0, 0.f, cu_seqlens, nseg, T,
-                              H, D, in_dtype, out, ws, FRATTN_NOALLOC_SCRATCH_BYTES, status,
-                              stream);
+                              H, D, in_dtype, out, ws, need, status, stream);
 }
 
 int frattn_set_wait_limit_ns(uint64_t limit_ns) {

@@ -51,7 +51,8 @@ enum {
 enum {
   FRATTN_STATUS_OK = 0,
   FRATTN_STATUS_WAIT_TIMEOUT = 0x100, /* | role << 4 | barrier group        */
-  FRATTN_STATUS_BAD_SEQLENS = 0x200   /* cu_seqlens not non-decreasing in [0,T] */
+  FRATTN_STATUS_BAD_SEQLENS = 0x200,  /* cu_seqlens not non-decreasing in [0,T] */
+  FRATTN_STATUS_BAD_POSITIONS = 0x400 /* a pos_hw value outside [0, max_position) */
 };
 
 /* Library version (major * 10000 + minor * 100 + patch). */
@@ -107,9 +108,11 @@ int frattn_fwd(const void* q, const void* k, const void* v, const void* cos, con
  *   inv_freq[i] = theta^(-2i / (D/2)),  i < D/4
  *   angle[t, i]        = pos_hw[t, 0] * inv_freq[i]   (i < D/4)
  *   angle[t, D/4 + i]  = pos_hw[t, 1] * inv_freq[i]
- *   pos_hw : [T, 2] int32, 0 <= value < 65536.
- * The per-position cos/sin table lives in the workspace, so this entry point
- * needs frattn_workspace_bytes_pos(...) bytes instead. */
+ *   pos_hw : [T, 2] int32, 0 <= value < max_position (max_position <= 65536).
+ * The per-position cos/sin table (max_position rows) lives in the workspace, so
+ * this entry point needs frattn_workspace_bytes_pos(...) bytes instead. The
+ * scheduler kernel checks every position against the table; on a value outside
+ * it nothing is computed and *status is set to FRATTN_STATUS_BAD_POSITIONS. */
 int frattn_workspace_bytes_pos(int total_tokens, int num_segments, int max_position, int D,
                                size_t* bytes);
 int frattn_fwd_pos(const void* q, const void* k, const void* v, const int32_t* pos_hw,
@@ -133,8 +136,13 @@ int frattn_fwd_pos(const void* q, const void* k, const void* v, const int32_t* p
  * Limits and rules:
  *   - T (total_tokens) <= FRATTN_NOALLOC_MAX_TOKENS, else FRATTN_E_NOALLOC_LIMIT;
  *   - the first call on a device looks up the array's device address (once,
- *     with that device current); make that first call before any stream
- *     capture;
+ *     with that device current) and caches it; make that first call before any
+ *     stream capture. A cudaDeviceReset destroys the array with the context,
+ *     and the cached address then no longer names it: do not call this entry
+ *     point on a device after resetting it;
+ *   - all rotation runs inside the attention kernel (the array never holds a
+ *     rotated-K copy); for long segments this is slower than frattn_fwd with a
+ *     rotated-K workspace;
  *   - every call on a device shares the one array: calls whose kernels overlap
  *     on the GPU (e.g. on two streams without ordering) race and may produce
  *     wrong output. Order such calls on one stream or use frattn_fwd.

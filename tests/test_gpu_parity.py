@@ -153,6 +153,22 @@ def test_bad_cu_seqlens_sets_status():
     assert last_status() == 0  # reset after reading
 
 
+def test_out_of_table_positions_set_status():
+    # A coordinate equal to max_position is one row past the rotary table. The
+    # scheduler kernel rejects it before any kernel reads the table (nothing is
+    # computed). Were the check missing, the read would still land inside the
+    # workspace (the sin half follows the cos half), so the case cannot fault.
+    q, k, v, _, _, cu = [t.to(DEV) for t in cu_case([0, 64, 300], H=2, seed=3)]
+    pos = torch.randint(0, 16, (300, 2), dtype=torch.int32, device=DEV)
+    fused_rope_attention_pos(q, k, v, pos, cu, max_position=16)
+    torch.cuda.synchronize()
+    assert last_status() == 0
+    pos[17, 1] = 16
+    fused_rope_attention_pos(q, k, v, pos, cu, max_position=16)
+    torch.cuda.synchronize()
+    assert last_status() == 0x400
+
+
 def test_device_wait_timeout_is_reported_not_hung():
     from fused_rope_attn_b200 import _lib
     st = torch.zeros(1, dtype=torch.int32, device=DEV)
