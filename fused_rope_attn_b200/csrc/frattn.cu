@@ -131,6 +131,20 @@ struct Ctl {
   int abort;
 };
 
+// Timeline trace (build with -DFRATTN_TRACE): SM clock stamps of pipeline
+// events of CTA 0's first two units, read back with frattn_trace_read.
+#ifdef FRATTN_TRACE
+constexpr int kTraceWords = 8192;
+__device__ unsigned long long g_trace[kTraceWords];
+#define FR_TRACE(ui, ev, idx)                                                          \
+  do {                                                                                 \
+    if (blockIdx.x == 0 && (ui) < 2 && (idx) < 128)                                    \
+      g_trace[(ui) * 4096 + (ev) * 128 + (idx)] = clock64();                           \
+  } while (0)
+#else
+#define FR_TRACE(ui, ev, idx) do { } while (0)
+#endif
+
 __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity, const Params& p,
                                              volatile int* abort_flag, int code) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -805,6 +819,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
             ok = bounded_wait(bar(B::K_EMPTY + ks), ((k_it / ST) & 1) ^ 1, p, abort_flag,
                               FRATTN_STATUS_WAIT_TIMEOUT | 0x01);
             if (!ok) break;
+            FR_TRACE((u - (int)blockIdx.x) / (int)gridDim.x, 0, j * 2 + x);
             mbar_arrive_expect_tx(bar(B::K_FULL + ks), C::TILE_BYTES);
 #pragma unroll
             for (int b = 0; b < C::KB; ++b)
@@ -831,6 +846,8 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
         bool ok = true;
         for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
           const Unit U = decode_unit(p, u, n_long);
+          const int ui = (u - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x);
+          (void)ui;
           const int ns = U.has_b ? 2 : 1;
           const int nk = U.shared ? 1 : ns;
           const int nkv = (U.kv1 - U.kv0 + kTileN - 1) / kTileN;
@@ -854,11 +871,13 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
                 ok = bounded_wait(bar(B::P_FULL + x), p_it[x] & 1, p, abort_flag,
                                   FRATTN_STATUS_WAIT_TIMEOUT | 0x11);
                 if (!ok) break;
+                FR_TRACE(ui, 1, (j - 1) * 2 + x);
                 ++p_it[x];
                 const uint32_t vi = vprev[x];
                 ok = bounded_wait(bar(B::V_FULL + vi % ST), (vi / ST) & 1, p, abort_flag,
                                   FRATTN_STATUS_WAIT_TIMEOUT | 0x12);
                 if (!ok) break;
+                FR_TRACE(ui, 2, (j - 1) * 2 + x);
                 tc_fence_after();
                 const uint32_t vaddr = sbase + C::OFF_V + (vi % ST) * C::TILE_BYTES;
                 const uint64_t vdesc = make_sdesc(vaddr, kBlkBytes, 256, SW32);
@@ -869,6 +888,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
                   umma_ts(tmem + C::TMEM_O + 128u * x, s_col + kk * 8, bd, IDESC_O,
                           (j > 1 || kk > 0) ? 1u : 0u);
                 }
+                FR_TRACE(ui, 10, (j - 1) * 2 + x);
                 if (!U.shared || x == ns - 1) umma_commit(bar(B::V_EMPTY + vi % ST));
                 if (j == nkv) umma_commit(bar(B::O_FULL + x));
               }
@@ -878,6 +898,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
                 ok = bounded_wait(bar(B::K_READY + ki % ST), (ki / ST) & 1, p, abort_flag,
                                   FRATTN_STATUS_WAIT_TIMEOUT | 0x13);
                 if (!ok) break;
+                FR_TRACE(ui, 3, j * 2 + x);
                 tc_fence_after();
                 const uint32_t qaddr = sbase + qbuf(x, qs[x]);
                 const uint32_t kaddr = sbase + C::OFF_K + (ki % ST) * C::TILE_BYTES;
@@ -893,7 +914,9 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
                     umma_ss(s_col, ad, bd, IDESC_S, kb > 0 ? 1u : 0u);
                   }
                 }
+                FR_TRACE(ui, 11, j * 2 + x);
                 umma_commit(bar(B::S_FULL + x));
+                FR_TRACE(ui, 4, j * 2 + x);
                 if (!U.shared || x == ns - 1) umma_commit(bar(B::K_EMPTY + ki % ST));
                 if (j == nkv - 1)
                   umma_commit(bar(C::Q_TMEM ? B::QT_FREE + x : B::Q_EMPTY + x * QB + qs[x]));
@@ -999,6 +1022,8 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
     bool ok = true;
     for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
       const Unit U = decode_unit(p, u, n_long);
+      const int ui = (u - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x);
+      (void)ui;
       if (x == 1 && !U.has_b) continue;
       const int h = x ? U.hb : U.ha;
       const int q0x = x ? U.q0b : U.q0a;
@@ -1021,6 +1046,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
         ok = bounded_wait_warp(bar(B::S_FULL + x), s_it & 1, p, abort_flag,
                                FRATTN_STATUS_WAIT_TIMEOUT | 0x30);
         if (!ok) break;
+        if (t == 0) FR_TRACE(ui, 5, j * 2 + x);
         ++s_it;
         tc_fence_after();
         float s[kTileN];
@@ -1032,6 +1058,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
           for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(rr[e]);
         }
         tmem_ld_wait();
+        if (t == 0) FR_TRACE(ui, 6, j * 2 + x);
 
         const int c0 = U.kv0 + j * kTileN;
         const int lo_r = lo - c0, hi_r = hi - c0;
@@ -1105,9 +1132,11 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
             tmem_st16(o_addr + c * 16, rr);
           }
         }
+        if (t == 0) FR_TRACE(ui, 7, j * 2 + x);
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(bar(B::P_FULL + x));
+        if (t == 0) FR_TRACE(ui, 8, j * 2 + x);
       }
       if (!ok) break;
       // Epilogue: last PV of this slot done -> normalise and store the row.
@@ -1115,6 +1144,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
                              FRATTN_STATUS_WAIT_TIMEOUT | 0x32);
       if (!ok) break;
       ++o_it;
+      if (t == 0) FR_TRACE(ui, 9, x);
       tc_fence_after();
       const bool store = lo < hi;
       const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
@@ -1468,24 +1498,36 @@ int launch_attn(const Params& prm, cudaStream_t st) {
 
 template <int D, int MODE, typename TI>
 int dispatch_cs(const Params& prm, int cs_dtype, cudaStream_t st) {
-  if (MODE == kRopePos) return launch_attn<D, MODE, TI, float>(prm, st);
+  if constexpr (MODE == kRopePos) return launch_attn<D, MODE, TI, float>(prm, st);
+#ifdef FRATTN_FAST_BUILD  // experiment builds: fp32 tables only
+  if (cs_dtype != FRATTN_F32) return FRATTN_E_DTYPE;
+  return launch_attn<D, MODE, TI, float>(prm, st);
+#else
   switch (cs_dtype) {
     case FRATTN_F32: return launch_attn<D, MODE, TI, float>(prm, st);
     case FRATTN_BF16: return launch_attn<D, MODE, TI, __nv_bfloat16>(prm, st);
     case FRATTN_F16: return launch_attn<D, MODE, TI, __half>(prm, st);
     default: return FRATTN_E_DTYPE;
   }
+#endif
 }
 
 template <int D, int MODE>
 int dispatch_in(const Params& prm, int in_dtype, int cs_dtype, cudaStream_t st) {
   if (in_dtype == FRATTN_BF16) return dispatch_cs<D, MODE, __nv_bfloat16>(prm, cs_dtype, st);
+#ifndef FRATTN_FAST_BUILD
   if (in_dtype == FRATTN_F16) return dispatch_cs<D, MODE, __half>(prm, cs_dtype, st);
+#endif
   return FRATTN_E_DTYPE;
 }
 
 template <int MODE>
 int dispatch_d(const Params& prm, int D, int in_dtype, int cs_dtype, cudaStream_t st) {
+#ifdef FRATTN_FAST_BUILD  // experiment builds: D = 80, table mode only
+  if (D != 80) return FRATTN_E_SHAPE;
+  if constexpr (MODE == kRopeTable) return dispatch_in<80, kRopeTable>(prm, in_dtype, cs_dtype, st);
+  return FRATTN_E_SHAPE;
+#else
   switch (D) {
     case 64: return dispatch_in<64, MODE>(prm, in_dtype, cs_dtype, st);
     case 72: return dispatch_in<72, MODE>(prm, in_dtype, cs_dtype, st);
@@ -1494,6 +1536,7 @@ int dispatch_d(const Params& prm, int D, int in_dtype, int cs_dtype, cudaStream_
     case 128: return dispatch_in<128, MODE>(prm, in_dtype, cs_dtype, st);
     default: return FRATTN_E_SHAPE;
   }
+#endif
 }
 
 template <typename TI>
@@ -1741,6 +1784,13 @@ int frattn_fwd_noalloc(const void* q, const void* k, const void* v, const void* 
   return fwd_impl<kRopeTable>(q, k, v, cos, sin, cs_dtype, nullptr, 0, 0.f, cu_seqlens, nseg, T,
                               H, D, in_dtype, out, ws, need, status, stream);
 }
+
+#ifdef FRATTN_TRACE
+int frattn_trace_read(unsigned long long* host, int words) {
+  if (words > kTraceWords) words = kTraceWords;
+  return cudaMemcpyFromSymbol(host, g_trace, words * sizeof(unsigned long long)) == cudaSuccess ? 0 : 1;
+}
+#endif
 
 int frattn_set_wait_limit_ns(uint64_t limit_ns) {
   if (limit_ns == 0) return FRATTN_E_SHAPE;
