@@ -148,6 +148,16 @@ def make_inputs(torch, device, seed, pin=False):
     return sets, T
 
 
+def bench_config(world: int) -> dict:
+    """The workload description both arms (ours and --impl reference) report."""
+    return {
+        "workload": WORKLOAD, "tokens_per_step": 4096, "heads": HEADS, "head_dim": HEAD_DIM,
+        "cos_sin_dtype": "fp32", "parallelism": f"dp{world} (independent images per rank)",
+        "l2": "8 rotating input sets (~350 MB) > 126 MB L2; no flush",
+        "max_seqlen": "passed as a hint (longest segment of the layer)",
+    }
+
+
 def algorithmic(cu, T, cs_bytes=4, io_bytes=2):
     """FLOPs = 4 * sum(L^2) * H * D; bytes = q,k,v read + out written + cos/sin read once + cu."""
     flops = 4 * sum((b - a) ** 2 for a, b in zip(cu[:-1], cu[1:]) if b > a) * HEADS * HEAD_DIM
@@ -226,7 +236,10 @@ def run_reference(args):
         return
     K, W = args.steps, args.warmup
     c = CpuOracleStep()
-    rows = c.rows_for(max(0.01, min(2.0, 120.0 / max(1, K + W))))
+    # Every step is the whole workload (all 4096 query rows of both layers)
+    # unless K + W full steps would take more than ~3 minutes; only then is
+    # each step a row sample scaled to the full step.
+    rows = c.rows_for(max(0.01, 180.0 / max(1, K + W)))
     for _ in range(W):
         c.run(rows)
     t0 = time.perf_counter()
@@ -239,9 +252,9 @@ def run_reference(args):
         "steps": K, "warmup": W, "ms_per_step": 4096 / value * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": WORKLOAD, "heads": HEADS, "head_dim": HEAD_DIM, "tokens_per_step": 4096,
-                   "path": "reference unfused path (RoPE bench.py:73-78 + per-segment attention utils.py:178-193) "
-                           "restated in numpy fp32 on the host cores (the reference itself is a GPU-only Triton kernel)"},
+        "config": bench_config(int(os.environ.get("WORLD_SIZE", "1"))),
+        "path": "reference unfused path (RoPE bench.py:73-78 + per-segment attention utils.py:178-193) "
+                "restated in numpy fp32 on the host cores (the reference itself is a GPU-only Triton kernel)",
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "wall_s": wall,
@@ -436,13 +449,9 @@ def run_ours(args):
             "metric": "vision_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K,
             "warmup": W, "ms_per_step": elapsed_ms / K, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) q/k/v, 2D RoPE tables)",
-            "config": {
-                "workload": WORKLOAD, "tokens_per_step": T, "heads": HEADS, "head_dim": HEAD_DIM,
-                "cos_sin_dtype": "fp32", "parallelism": f"dp{world} (independent images per rank)",
-                "l2": "8 rotating input sets (~350 MB) > 126 MB L2; no flush",
-                "launch": "each layer call replayed from a CUDA graph (work list, K pre-rotation for long segments, attention kernel)",
-                "max_seqlen": "passed as a hint (longest segment of the layer)",
-            },
+            "config": bench_config(world),
+            "launch": "each layer call replayed from a CUDA graph (work list, K pre-rotation for long segments, "
+                      "attention kernel)",
             # work list + attention per call, + the K pre-rotation when a segment is long
             "gpu_launches": K * sum(2 + (hint[var] > 128) for var in variants),
             "layer_us": {var: per_var[var] * 1e3 for var in variants},

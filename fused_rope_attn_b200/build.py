@@ -1,8 +1,12 @@
 """Build ``libfrattn.so`` in-tree with nvcc for sm_100a.
 
 ``python -m fused_rope_attn_b200.build`` (or ``__graft_entry__.build()``).
-The CUDA runtime is linked statically so the library loads on machines
-without a GPU (the C-ABI symbol test) and needs only the driver at run time.
+The kernels of each supported head dimension are compiled from
+``csrc/frattn_inst.cu`` into their own object (``-DFRATTN_D=<D>``), in
+parallel, and linked with the host code of ``csrc/frattn.cu`` into one shared
+library. The CUDA runtime is linked statically so the library loads on
+machines without a GPU (the C-ABI symbol test) and needs only the driver at
+run time.
 """
 from __future__ import annotations
 
@@ -10,17 +14,24 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
-SRC = os.path.join(HERE, "csrc", "frattn.cu")
-DEPS = [SRC, os.path.join(HERE, "csrc", "frattn_ptx.cuh"), os.path.join(ROOT, "include", "frattn.h")]
+CSRC = os.path.join(HERE, "csrc")
+HOST_SRC = os.path.join(CSRC, "frattn.cu")
+INST_SRC = os.path.join(CSRC, "frattn_inst.cu")
+DEPS = [HOST_SRC, INST_SRC, os.path.join(CSRC, "frattn_kernel.cuh"), os.path.join(CSRC, "frattn_ptx.cuh"),
+        os.path.join(ROOT, "include", "frattn.h")]
 OUT = os.path.join(HERE, "libfrattn.so")
+OBJ_DIR = os.path.join(HERE, "_build")
+
+HEAD_DIMS = tuple(range(32, 129, 8))  # must match FRATTN_HEAD_DIMS in csrc/frattn.cu
 
 NVCC_FLAGS = [
     "-std=c++17", "-O3", "-lineinfo",
     "-gencode", "arch=compute_100a,code=sm_100a",
-    "-Xcompiler", "-fPIC", "-shared", "-cudart", "static",
+    "-Xcompiler", "-fPIC",
     "-I", os.path.join(ROOT, "include"),
 ]
 
@@ -39,15 +50,33 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(d) <= t for d in DEPS)
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and up_to_date():
-        return OUT
-    tmp = OUT + ".tmp"
-    cmd = [nvcc(), *NVCC_FLAGS, "-o", tmp, SRC]
+def _run(cmd: list[str], verbose: bool) -> None:
     if verbose:
-        cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)
+
+
+def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -> str:
+    if not force and up_to_date():
+        return OUT
+    os.makedirs(OBJ_DIR, exist_ok=True)
+    extra = ["-Xptxas=-v"] if verbose else []
+    jobs = jobs or max(1, os.cpu_count() or 1)
+    cmds, objs = [], []
+    for d in HEAD_DIMS:
+        obj = os.path.join(OBJ_DIR, f"frattn_d{d}.o")
+        cmds.append([nvcc(), *NVCC_FLAGS, *extra, f"-DFRATTN_D={d}", "-c", "-o", obj, INST_SRC])
+        objs.append(obj)
+    host_obj = os.path.join(OBJ_DIR, "frattn_host.o")
+    cmds.append([nvcc(), *NVCC_FLAGS, *extra, "-c", "-o", host_obj, HOST_SRC])
+    objs.append(host_obj)
+    # the slowest objects first
+    with ThreadPoolExecutor(max_workers=jobs) as pool:
+        for f in [pool.submit(_run, c, verbose) for c in cmds]:
+            f.result()
+    tmp = OUT + ".tmp"
+    _run([nvcc(), "-shared", "-cudart", "static", "-gencode", "arch=compute_100a,code=sm_100a", "-o", tmp,
+          *objs], verbose)
     os.replace(tmp, OUT)
     return OUT
 

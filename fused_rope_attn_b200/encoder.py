@@ -30,7 +30,7 @@ import torch
 from .fused_attn import compute_rope_2d, fused_rope_attention
 from .utils import get_window_index, segments_per_image, window_shuffle, window_unshuffle
 
-__all__ = ["EncoderConfig", "VisionEncoder", "encoder_inputs", "rope_unfused"]
+__all__ = ["EncoderConfig", "VisionEncoder", "encoder_inputs", "rope_unfused", "attention_fp32"]
 
 
 @dataclass
@@ -60,17 +60,35 @@ def rope_unfused(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch
     return torch.cat([x0 * c - x1 * s, x0 * s + x1 * c], dim=-1)
 
 
-def _attn_fp32(q, k, v, cos, sin, cu):
+def attention_fp32(q, k, v, cos, sin, cu) -> torch.Tensor:
+    """RoPE then per-segment softmax attention, all in fp32 (fp32 result).
+
+    The reference's unfused path (bench.py:73-78 + utils.py:178-193) without any
+    rounding; runs of equal-length segments are batched into one call.
+    """
     qr = rope_unfused(q.float(), cos.float(), sin.float())
     kr = rope_unfused(k.float(), cos.float(), sin.float())
+    vf = v.float()
     out = torch.zeros_like(qr)
     cl = cu.tolist()
-    for a, b in zip(cl[:-1], cl[1:]):
-        if b > a:
-            out[a:b] = torch.nn.functional.scaled_dot_product_attention(
-                qr[a:b].transpose(0, 1), kr[a:b].transpose(0, 1), v[a:b].float().transpose(0, 1)
-            ).transpose(0, 1)
-    return out.to(q.dtype)
+    i, n = 0, len(cl) - 1
+    while i < n:
+        L = cl[i + 1] - cl[i]
+        j = i
+        while j < n and cl[j + 1] - cl[j] == L:
+            j += 1
+        a, b = cl[i], cl[j]
+        if L > 0:
+            def seg(x):  # [nseg * L, H, D] -> [nseg, H, L, D]
+                return x[a:b].reshape(j - i, L, *x.shape[1:]).transpose(1, 2)
+            o = torch.nn.functional.scaled_dot_product_attention(seg(qr), seg(kr), seg(vf))
+            out[a:b] = o.transpose(1, 2).reshape(b - a, *qr.shape[1:])
+        i = j
+    return out
+
+
+def _attn_fp32(q, k, v, cos, sin, cu):
+    return attention_fp32(q, k, v, cos, sin, cu).to(q.dtype)
 
 
 _FA_OK: bool | None = None
@@ -138,7 +156,11 @@ class VisionEncoder(torch.nn.Module):
         return dict(widx=widx.to(self.device), cu_win=cu_win.to(self.device), cu_full=cu_full.to(self.device),
                     max_win=int(lw), max_full=int(lf), cos=cos, sin=sin)
 
-    def forward(self, x: torch.Tensor, grid_thw, attn: str = "fused", plan=None, layer_hook=None):
+    def forward(self, x: torch.Tensor, grid_thw, attn: str = "fused", plan=None, layer_hook=None,
+                attn_hook=None):
+        """Run the stack. ``layer_hook(i, h)`` sees the hidden states after layer i;
+        ``attn_hook(i, q, k, v, cos, sin, cu_seqlens, o)`` sees each attention call's
+        inputs and output (window order)."""
         c = self.cfg
         plan = plan or self.plan(grid_thw)
         T = x.shape[0]
@@ -159,6 +181,8 @@ class VisionEncoder(torch.nn.Module):
                 o = _attn_fp32(q, k, v, plan["cos"], plan["sin"], cu)
             else:
                 raise ValueError(f"unknown attention implementation {attn!r}")
+            if attn_hook is not None:
+                attn_hook(i, q, k, v, plan["cos"], plan["sin"], cu, o)
             h = h + torch.nn.functional.linear(o.reshape(T, -1), L["proj_w"], L["proj_b"])
             y = self._rms(h, L["n2"])
             a = torch.nn.functional.silu(torch.nn.functional.linear(y, L["gate_w"])) * \

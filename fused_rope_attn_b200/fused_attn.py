@@ -38,7 +38,12 @@ __all__ = [
     "SUPPORTED_HEAD_DIMS",
 ]
 
-SUPPORTED_HEAD_DIMS = (64, 72, 80, 96, 128)
+# Head dimensions with compiled sm_100a kernels (multiples of 8 in [32, 128]).
+# Any other even head_dim up to 128 runs on the next one through zero padding
+# (``_padded_dim``), so every head_dim the reference accepts
+# (fused_attn.py:166-168) up to 128 works.
+KERNEL_HEAD_DIMS = tuple(range(32, 129, 8))
+SUPPORTED_HEAD_DIMS = tuple(range(2, 129, 2))
 
 _DT = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
 
@@ -219,7 +224,26 @@ def _check_out(out, q):
 
 def _check_head_dim(hd):
     if hd not in SUPPORTED_HEAD_DIMS:
-        raise ValueError(f"head_dim {hd} is not supported by the sm_100a kernel (supported: {SUPPORTED_HEAD_DIMS})")
+        raise ValueError(f"head_dim {hd} is not supported by the sm_100a kernel (even values up to 128)")
+
+
+def _padded_dim(hd: int) -> int:
+    """Kernel head dim for ``hd``: each rotate-half half padded to a multiple of 4, at least 32 in total."""
+    return max(32, 2 * (-(-(hd // 2) // 4) * 4))
+
+
+def _pad_halves(x: torch.Tensor, hd: int, dp: int) -> torch.Tensor:
+    """[..., hd] -> [..., dp] with x[:hd/2] at 0 and x[hd/2:] at dp/2, zeros elsewhere."""
+    h, hp = hd // 2, dp // 2
+    y = x.new_zeros(*x.shape[:-1], dp)
+    y[..., :h] = x[..., :h]
+    y[..., hp:hp + h] = x[..., h:]
+    return y
+
+
+def _unpad_halves(y: torch.Tensor, hd: int, dp: int) -> torch.Tensor:
+    h, hp = hd // 2, dp // 2
+    return torch.cat([y[..., :h], y[..., hp:hp + h]], dim=-1)
 
 
 def fused_rope_attention(
@@ -260,6 +284,25 @@ def fused_rope_attention(
     if sin.dtype != cos.dtype:
         sin = sin.to(cos.dtype)
     _check_head_dim(hd)
+    if hd not in KERNEL_HEAD_DIMS:
+        # Zero-pad each half of q/k/v to the kernel's head dim. Padded lanes
+        # contribute nothing to QK^T or PV; the kernel scales scores by
+        # 1/sqrt(dp), so cos/sin carry (dp/hd)^(1/4) each to restore
+        # 1/sqrt(hd) (fused_attn.py:355). Rotation stays in fp32.
+        dp = _padded_dim(hd)
+        f = (dp / hd) ** 0.25
+        cs = torch.ones(total, dp // 2, dtype=torch.float32, device=q.device)
+        sn = torch.zeros(total, dp // 2, dtype=torch.float32, device=q.device)
+        cs[:, : hd // 2] = cos.to(q.device, torch.float32)
+        sn[:, : hd // 2] = sin.to(q.device, torch.float32)
+        _check_out(out, q)
+        o = fused_rope_attention(_pad_halves(q, hd, dp), _pad_halves(k, hd, dp), _pad_halves(v, hd, dp),
+                                 cs * f, sn * f, cu_seqlens, max_seqlen=max_seqlen)
+        res = _unpad_halves(o, hd, dp)
+        if out is None:
+            return res.contiguous()
+        out.copy_(res)
+        return out
     q, k, v = (_aligned(t.contiguous()) for t in (q, k, v))
     cos = _aligned(cos.to(q.device).contiguous())
     sin = _aligned(sin.to(q.device).contiguous())
@@ -308,7 +351,8 @@ def fused_rope_attention_pos(
         raise ValueError(f"pos_hw must be [total_seq, 2]={total, 2}, got {tuple(pos_hw.shape)}")
     if hd % 4 != 0:
         raise ValueError(f"head_dim must be divisible by 4 for 2D RoPE, got {hd}")
-    _check_head_dim(hd)
+    if hd not in KERNEL_HEAD_DIMS:
+        raise ValueError(f"head_dim {hd} is not supported by the position entry point (multiples of 8 in [32, 128])")
     pos = _aligned(pos_hw.to(device=q.device, dtype=torch.int32).contiguous())
     if max_position is None:
         max_position = int(pos.max().item()) + 1 if total > 0 else 1

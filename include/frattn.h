@@ -95,7 +95,11 @@ int frattn_workspace_bytes_rotated_k(int total_tokens, int num_heads, int head_d
  *   stream       : cudaStream_t the kernels are launched on
  * Rows of `out` outside [cu[0], cu[nseg]) are written with zeros (this makes an
  * all-empty cu_seqlens return zeros, matching fused_attn.py:212-213).
- * Supported D: 64, 72, 80, 96, 128 (72 runs on 80-column tiles, zero-padded by TMA).
+ * Supported D: every multiple of 8 in [32, 128]. A D that is not a multiple of
+ * 16 runs on tiles rounded up to the next multiple of 16; TMA fills the extra
+ * columns with zeros, so they add nothing to QK^T and are never stored. (The
+ * Python wrapper reaches any other even D up to 128 by zero-padding each
+ * rotate-half half; this ABI takes the kernel dims only.)
  */
 int frattn_fwd(const void* q, const void* k, const void* v, const void* cos, const void* sin,
                int cs_dtype, const int32_t* cu_seqlens, int nseg, int T, int H, int D,

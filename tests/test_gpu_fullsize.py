@@ -1,4 +1,4 @@
-"""Full BASELINE sizes (1344x1344 image: 9216 tokens) through size-independent properties.
+"""Full BASELINE sizes (1344x1344 image: 9216 tokens; an 8192-token clip) through size-independent properties.
 
 Dense oracle comparison at these sizes is replaced by: a random subsample of query
 rows against the oracle, softmax normalisation (constant V per segment), linearity
@@ -17,9 +17,16 @@ DEV = "cuda"
 GRID = [(1, 96, 96)]
 
 
-@pytest.fixture(scope="module", params=[False, True], ids=["full9216", "windowed144x64"])
+# BASELINE config 5's clip: 16 frames of 448x448 with temporal patch 2 -> t = 8
+# frames of 32 x 32 patches, one 8192-token full-attention segment per clip.
+CLIP = [(8, 32, 32)]
+
+
+@pytest.fixture(scope="module", params=[(GRID, False), (GRID, True), (CLIP, False)],
+                ids=["full9216", "windowed144x64", "clip8192"])
 def case(request):
-    q, k, v, cos, sin, cu = grid_case(GRID, request.param, seed=44)
+    grid, windowed = request.param
+    q, k, v, cos, sin, cu = grid_case(grid, windowed, seed=44)
     return [t.to(DEV) for t in (q, k, v, cos, sin, cu)]
 
 

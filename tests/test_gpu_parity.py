@@ -64,10 +64,24 @@ def test_dtypes(dtype, cs_dtype):
     assert_close(run(*case), oracle(*case))
 
 
-@pytest.mark.parametrize("D", [64, 72, 80, 96, 128])
+@pytest.mark.parametrize("D", list(range(32, 129, 8)))
 def test_head_dims(D):
+    """Every compiled kernel head dim (multiples of 8 in [32, 128])."""
     case = cu_case([0, 64, 128, 390, 400], H=2, D=D, seed=D)
     assert_close(run(*case), oracle(*case))
+
+
+@pytest.mark.parametrize("D", [2, 16, 36, 50, 124])
+def test_padded_head_dims(D):
+    """Other even head dims (the reference accepts any even D, fused_attn.py:166-168)
+    run on the next kernel dim through zero padding; the result is unpadded."""
+    case = cu_case([0, 64, 300, 301], H=3, D=D, seed=D + 1)
+    out = run(*case)
+    assert out.shape == case[0].shape
+    assert_close(out, oracle(*case))
+    o2 = torch.empty_like(case[0], device=DEV)
+    run(*case, out=o2)
+    assert torch.equal(o2, out)
 
 
 @pytest.mark.parametrize("cu_list", [
