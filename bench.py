@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=100)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-encoder", action="store_true", help="skip the 32-layer encoder timing")
+    ap.add_argument("--no-dp", action="store_true", help="skip the config-5 data-parallel sweep")
+    ap.add_argument("--no-comparators", action="store_true", help="skip the same-box GPU comparators")
     return ap.parse_args()
 
 
@@ -303,6 +305,114 @@ def encoder_timing(torch, dev, reps=10):
             "fused_vs_unfused_rel_l2": rel_l2(outs["fused"], outs["unfused"]), "launch": "CUDA graph replay"}
 
 
+# --------------------------------------------------------------------------- config 5
+DP_GRIDS = [(1, 64, 64)] * 64 + [(8, 32, 32)] * 8  # 64 images 896x896 + 8 clips (16 frames 448x448, t=8)
+
+
+def dp_sweep(torch, dist, dev, world, rank, reps=2):
+    """BASELINE config 5 through ``dp.run_dp``: the 72 items are LPT-partitioned
+    over the ranks, every rank runs the 32-layer encoder (fused attention) on its
+    packed items, and the outputs are gathered to rank 0 (NCCL). Inputs and the
+    window plan are prepared before timing; each timed pass = encoder + gather,
+    CUDA events on every rank, the pass time is the max over ranks."""
+    from fused_rope_attn_b200.dp import item_cost, local_inputs, partition, run_dp
+    from fused_rope_attn_b200.encoder import EncoderConfig, VisionEncoder
+    cfg = EncoderConfig()
+    enc = VisionEncoder(cfg, device=dev, dtype=torch.bfloat16)
+    costs = [item_cost(g, cfg) for g in DP_GRIDS]
+    parts = partition(costs, world)
+    x, my_grids = local_inputs(enc, DP_GRIDS, parts, rank, seed=5)
+    plan = enc.plan(my_grids) if my_grids else None
+    total_tokens = sum(t * h * w for t, h, w in DP_GRIDS)
+    run_dp(enc, DP_GRIDS, inputs=(x, my_grids), plan=plan)  # warm-up
+    torch.cuda.synchronize()
+    comp, gath, tot = [], [], []
+    for _ in range(reps):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        dist.barrier()
+        torch.cuda.synchronize()
+        run_dp(enc, DP_GRIDS, inputs=(x, my_grids), plan=plan, events=ev)
+        torch.cuda.synchronize()
+        t = torch.tensor([ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]), ev[0].elapsed_time(ev[2])],
+                         device=dev)
+        allt = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(allt, t)
+        allt = torch.stack(allt).cpu()
+        comp.append(allt[:, 0].tolist())
+        gath.append(allt[:, 1].tolist())
+        tot.append(float(allt[:, 2].max()))
+    best = min(range(reps), key=lambda i: tot[i])
+    c = comp[best]
+    loads = [sum(costs[i] for i in p) for p in parts]
+    return {
+        "items": "64 images 896x896 (4096 tokens) + 8 clips 16x448x448, t=8 (8192 tokens)",
+        "tokens": total_tokens, "pass_ms": tot[best], "tokens_per_s": total_tokens / (tot[best] / 1e3),
+        "rank_encoder_ms": c, "rank_gather_ms": gath[best],
+        "gather_share": max(gath[best]) / tot[best],
+        "imbalance_measured": max(c) / max(1e-9, min(c)) if min(c) > 0 else None,
+        "imbalance_model": max(loads) / max(1e-9, min(loads)) if min(loads) > 0 else None,
+        "timing": "CUDA events per rank (encoder, gather), pass = max over ranks, best of %d" % reps,
+    }
+
+
+# --------------------------------------------------------------------------- same-box GPU comparators
+def gpu_comparators(torch, sets, hint, ours_us, reps=20):
+    """The config-2 layers through (a) the reference's own Triton kernel
+    (``fused_rope_attention`` of fused_attn.py, installed unmodified into
+    baseline/_ref, autotuned by Triton on this GPU) and (b) the reference's
+    baseline path, separate bf16 RoPE + ``flash_attn_varlen_func``
+    (bench.py:72-86). Per-call µs with CUDA events after warm-up, rotating the
+    same input sets as the timed graphs (eager calls: the reference's wrapper
+    syncs on the host every call)."""
+    import importlib.util
+    from fused_rope_attn_b200.encoder import _attn_unfused, unfused_backend
+    out = {}
+    ref = None
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    try:
+        spec = importlib.util.spec_from_file_location("frattn_reference_fused_attn",
+                                                      os.path.join(ref_dir, "fused_attn.py"))
+        ref = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(ref)
+    except Exception as exc:  # noqa: BLE001
+        out["reference_triton"] = f"unavailable: {type(exc).__name__}: {exc}"[:200]
+    R = len(sets)
+
+    def timeit(fn):
+        for i in range(3):
+            fn(sets[i % R])
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(reps):
+            fn(sets[i % R])
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps * 1e3
+
+    for var in ("windowed", "full"):
+        row = {"ours_us": ours_us[var]}
+        if ref is not None:
+            try:
+                row["reference_triton_us"] = timeit(lambda s: ref.fused_rope_attention(
+                    s[var]["q"], s[var]["k"], s[var]["v"], s[var]["cos"], s[var]["sin"], s[var]["cu"]))
+                t = sets[0][var]
+                o_ref = ref.fused_rope_attention(t["q"], t["k"], t["v"], t["cos"], t["sin"], t["cu"])
+                row["reference_vs_ours_max_abs"] = (o_ref.float() - t["out"].float()).abs().max().item()
+                row["speedup_vs_reference_triton"] = row["reference_triton_us"] / ours_us[var]
+            except Exception as exc:  # noqa: BLE001
+                row["reference_triton"] = f"error: {type(exc).__name__}: {exc}"[:200]
+        try:
+            row["rope_plus_varlen_us"] = timeit(lambda s: _attn_unfused(
+                s[var]["q"], s[var]["k"], s[var]["v"], s[var]["cos"], s[var]["sin"], s[var]["cu"], hint[var]))
+            row["varlen_backend"] = unfused_backend()
+            row["speedup_vs_rope_plus_varlen"] = row["rope_plus_varlen_us"] / ours_us[var]
+        except Exception as exc:  # noqa: BLE001
+            row["rope_plus_varlen"] = f"error: {type(exc).__name__}: {exc}"[:200]
+        out[var] = row
+    return out
+
+
 # --------------------------------------------------------------------------- GPU
 def run_ours(args):
     import torch
@@ -316,6 +426,15 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
+    elif not args.no_dp:
+        # one-rank group, so that the config-5 sweep runs the same code at N = 1
+        import socket
+        sk = socket.socket()
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+        sk.close()
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1,
+                                device_id=dev)
 
     def barrier():
         if world > 1:
@@ -438,6 +557,13 @@ def run_ours(args):
         e2e_ms = float(t.item())
     e2e_value = world * T * E / (e2e_ms / 1e3)
 
+    dp_res = None
+    if not args.no_dp:
+        try:
+            dp_res = dp_sweep(torch, dist, dev, world, rank)
+        except Exception as exc:  # noqa: BLE001 - report, do not lose the main line
+            dp_res = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+
     if rank == 0:
         hbm, tflops, src = load_peaks()
         traffic = load_traffic()
@@ -467,6 +593,14 @@ def run_ours(args):
             "clocks": clk,
             "device_status": status,
         }
+        if dp_res is not None:
+            line["dp_sweep"] = dp_res
+        if not args.no_comparators:
+            try:
+                line["gpu_comparators"] = gpu_comparators(torch, sets, hint,
+                                                          {v: per_var[v] * 1e3 for v in variants})
+            except Exception as exc:  # noqa: BLE001
+                line["gpu_comparators"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
         if not args.no_encoder:
             try:
                 line["encoder"] = encoder_timing(torch, dev)
@@ -476,7 +610,7 @@ def run_ours(args):
             v, cores, sample = cpu_baseline(budget_s=10.0)
             line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
         print(json.dumps(line), flush=True)
-    if world > 1:
+    if dist.is_initialized():
         dist.barrier()
         dist.destroy_process_group()
 

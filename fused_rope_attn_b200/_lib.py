@@ -34,6 +34,10 @@ _SIGNATURES = {
     "frattn_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _sz, _vp, _vp]),
     "frattn_fwd_pos": (_i, [_vp, _vp, _vp, _vp, _i, _f, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _sz, _vp, _vp]),
     "frattn_fwd_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
+    "frattn_window_plan_sizes": (_i, [_vp, _i, _i, _i, _i, ctypes.POINTER(ctypes.c_int64),
+                                      ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(_sz)]),
+    "frattn_window_plan": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _i, _f, _vp, _sz, _vp]),
+    "frattn_window_shuffle": (_i, [_vp, _vp, ctypes.c_int64, _i, ctypes.c_int64, _i, _vp, _vp]),
     "frattn_selftest_wait_timeout": (_i, [_vp, _u64, _vp]),
     "frattn_set_wait_limit_ns": (_i, [_u64]),
 }

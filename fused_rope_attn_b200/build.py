@@ -21,7 +21,8 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 HOST_SRC = os.path.join(CSRC, "frattn.cu")
 INST_SRC = os.path.join(CSRC, "frattn_inst.cu")
-DEPS = [HOST_SRC, INST_SRC, os.path.join(CSRC, "frattn_kernel.cuh"), os.path.join(CSRC, "frattn_ptx.cuh"),
+WINDOW_SRC = os.path.join(CSRC, "frattn_window.cu")
+DEPS = [HOST_SRC, INST_SRC, WINDOW_SRC, os.path.join(CSRC, "frattn_kernel.cuh"), os.path.join(CSRC, "frattn_ptx.cuh"),
         os.path.join(ROOT, "include", "frattn.h")]
 OUT = os.path.join(HERE, "libfrattn.so")
 OBJ_DIR = os.path.join(HERE, "_build")
@@ -67,6 +68,9 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -
         obj = os.path.join(OBJ_DIR, f"frattn_d{d}.o")
         cmds.append([nvcc(), *NVCC_FLAGS, *extra, f"-DFRATTN_D={d}", "-c", "-o", obj, INST_SRC])
         objs.append(obj)
+    win_obj = os.path.join(OBJ_DIR, "frattn_window.o")
+    cmds.append([nvcc(), *NVCC_FLAGS, *extra, "-c", "-o", win_obj, WINDOW_SRC])
+    objs.append(win_obj)
     host_obj = os.path.join(OBJ_DIR, "frattn_host.o")
     cmds.append([nvcc(), *NVCC_FLAGS, *extra, "-c", "-o", host_obj, HOST_SRC])
     objs.append(host_obj)

@@ -12,6 +12,7 @@ namespace frattn {
 
 #define FRATTN_DECL(DD)                                                                       \
   int attn_d##DD(const Params& prm, int mode, int in_dtype, int cs_dtype, cudaStream_t st);   \
+  int window_d##DD(const Params& prm, int in_dtype, int cs_dtype, cudaStream_t st);            \
   int prep_d##DD(const int32_t* cu, int nseg, int T, int H, WorkItem* items, int* header,     \
                  void* out, int32_t* status, const int32_t* pos_hw, float* pos_tab,           \
                  int pos_rows, float theta, int in_dtype, cudaStream_t st);
@@ -119,6 +120,21 @@ int dispatch_head_dim(const Params& prm, int mode, int D, int in_dtype, int cs_d
   }
 }
 
+// Window kernel of head dimension D (FRATTN_E_SHAPE: none for this D / type).
+int dispatch_window(const Params& prm, int D, int in_dtype, int cs_dtype, cudaStream_t st) {
+  switch (D) {
+#define FRATTN_CASE(DD) \
+    case DD: return window_d##DD(prm, in_dtype, cs_dtype, st);
+#ifdef FRATTN_FAST_BUILD
+    FRATTN_CASE(80)
+#else
+    FRATTN_HEAD_DIMS(FRATTN_CASE)
+#endif
+#undef FRATTN_CASE
+    default: return FRATTN_E_SHAPE;
+  }
+}
+
 // Work-list kernel of head dimension D.
 int launch_prep(const int32_t* cu, int nseg, int T, int H, int D, WorkItem* items, int* header,
                 void* out, int32_t* status, const int32_t* pos_hw, float* pos_tab, int pos_rows,
@@ -195,10 +211,9 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
     base = (base + 255) & ~size_t(255);
     pos_tab = reinterpret_cast<float*>(ws + base);
   }
-  rc = launch_prep(cu, nseg, T, H, D, items, header, out, status, pos_hw, pos_tab, max_position,
-                   theta, in_dtype, st);
-  if (rc) return rc;
-  if (T == 0) return 0;
+  if (T == 0)
+    return launch_prep(cu, nseg, T, H, D, items, header, out, status, pos_hw, pos_tab,
+                       max_position, theta, in_dtype, st);
 
   Params prm;
   memset(&prm, 0, sizeof(prm));
@@ -239,6 +254,16 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
   prm.H = H;
   prm.status = status;
   prm.wait_limit_ns = g_wait_limit_ns;
+  // Window regime (the caller says no segment exceeds one tile): one kernel,
+  // no work list. Head dims / element types without a window kernel, and the
+  // position entry point, take the general path below.
+  if (MODE == kRopeTable && no_long) {
+    rc = dispatch_window(prm, D, in_dtype, cs_dtype, st);
+    if (rc != FRATTN_E_SHAPE) return rc;
+  }
+  rc = launch_prep(cu, nseg, T, H, D, items, header, out, status, pos_hw, pos_tab, max_position,
+                   theta, in_dtype, st);
+  if (rc) return rc;
   return dispatch_head_dim(prm, MODE, D, in_dtype, cs_dtype, st);
 }
 

@@ -23,6 +23,16 @@ int FRATTN_CAT(attn_d, FRATTN_D)(const Params& prm, int mode, int in_dtype, int 
 #endif
 }
 
+// Window-regime kernel (every segment at most 128 tokens); FRATTN_E_SHAPE when
+// this head dim or element type has none.
+int FRATTN_CAT(window_d, FRATTN_D)(const Params& prm, int in_dtype, int cs_dtype, cudaStream_t st) {
+  if (in_dtype == FRATTN_BF16) return window_cs<FRATTN_D, __nv_bfloat16>(prm, cs_dtype, st);
+#ifndef FRATTN_FAST_BUILD
+  if (in_dtype == FRATTN_F16) return window_cs<FRATTN_D, __half>(prm, cs_dtype, st);
+#endif
+  return FRATTN_E_DTYPE;
+}
+
 // Work-list (scheduler) kernel of this head dimension.
 int FRATTN_CAT(prep_d, FRATTN_D)(const int32_t* cu, int nseg, int T, int H, WorkItem* items,
                                  int* header, void* out, int32_t* status, const int32_t* pos_hw,

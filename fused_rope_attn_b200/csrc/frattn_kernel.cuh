@@ -1442,4 +1442,535 @@ int dispatch_in(const Params& prm, int in_dtype, int cs_dtype, cudaStream_t st) 
   return FRATTN_E_DTYPE;
 }
 
+// ------------------------------------------------------------------ window kernel
+// Window regime (every segment at most one tile long, e.g. the 8x8-patch
+// windows of the vision tower): one CTA per (128-row chunk of the packed
+// sequence, head), no work list and no persistent loop. Two CTAs share an SM
+// (256 TMEM columns each), so the hardware overlaps one CTA's loads with the
+// other's rotation, MMAs and softmax. The chunk's q rows attend to the
+// segments that contain them: kv rows [kv0, kv1) from the first to the last of
+// those segments, in 128-row K/V tiles (online softmax over the tiles, so any
+// segmentation is handled; windows of up to 64 tokens give one tile).
+// 128 threads, one q row each: RoPE of its Q row (into TMEM) and K row (in
+// shared memory), softmax of its row, epilogue. Thread 0 also issues the TMA
+// loads and the tcgen05 MMAs; the phases of a tile are separated by CTA
+// barriers (the work of a CTA is one serial chain; overlap comes from the
+// other CTA on the SM). 128 threads, because registers are charged per four
+// warps: a fifth warp would cost a whole second group and halve residency.
+constexpr int kWinThreads = 128;
+constexpr int kWinStage = 1024;  // cu_seqlens entries staged in shared memory
+
+// First index i in [0, n) with v[i] > x (n if none), v non-decreasing.
+__device__ __forceinline__ int upper_bound_smem(const int* v, int n, int x) {
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (v[mid] > x) hi = mid; else lo = mid + 1;
+  }
+  return lo;
+}
+
+// First index i in [0, n) with cu[i] > x (n if none), cu non-decreasing: a
+// 32-way search by one warp (every lane returns the result).
+__device__ __forceinline__ int warp_upper_bound(const int32_t* cu, int n, int x, int lane) {
+  int lo = 0, hi = n;  // the answer lies in [lo, hi]
+  while (hi - lo > 32) {
+    const int step = (hi - lo + 31) / 32;
+    const int idx = lo + lane * step;
+    const bool gt = idx >= hi || __ldg(cu + idx) > x;  // probes past the range count as above
+    const uint32_t m = __ballot_sync(0xffffffffu, gt);
+    const int f = m ? __ffs(m) - 1 : 32;  // first probe above x
+    if (f == 0) return lo;
+    const int nlo = lo + (f - 1) * step + 1;
+    hi = f < 32 ? min(hi, lo + f * step) : hi;
+    lo = nlo;
+  }
+  const int idx = lo + lane;
+  const bool gt = idx < hi && __ldg(cu + idx) > x;
+  const uint32_t m = __ballot_sync(0xffffffffu, gt);
+  return m ? lo + __ffs(m) - 1 : hi;
+}
+constexpr int kWinSmemMin = 80 * 1024;  // keeps at most two CTAs (512 TMEM columns) per SM
+
+template <int D, int CSB>
+struct WinCfg {
+  using C = Cfg<D, CSB>;
+  static_assert(C::Q_TMEM, "window kernel: Q lives in TMEM behind O");
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + C::TILE_BYTES;
+  static constexpr int OFF_V = OFF_K + C::TILE_BYTES;
+  static constexpr int OFF_BAR = OFF_V + C::TILE_BYTES;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int RAW = OFF_BAR + BAR_BYTES + 1024;  // +1024 alignment slack
+  static constexpr int SMEM_BYTES = RAW < kWinSmemMin ? kWinSmemMin : RAW;
+  static constexpr uint32_t TMEM_COLS = 256;
+  static constexpr uint32_t TMEM_S = 0;    // S / P
+  static constexpr uint32_t TMEM_O = 128;  // O (DP columns), rotated Q behind it
+  static constexpr uint32_t TMEM_Q = TMEM_O + C::DP;
+  static_assert(TMEM_Q + C::DP / 2 <= TMEM_COLS, "TMEM columns");
+  // barriers (all single-arrival: TMA transactions or tcgen05 commits)
+  static constexpr int Q_FULL = 0, K_FULL = 1, V_FULL = 2, S_FULL = 3, KV_EMPTY = 4, O_FULL = 5,
+                       COUNT = 6;
+};
+
+// Rotate row r of a raw 128 x D tile with cos/sin held in registers (fp32,
+// one rounding to the element type): into TMEM at column qcol as packed pairs
+// (TO_TMEM) or in place in shared memory.
+template <int D, typename TI, bool TO_TMEM>
+__device__ __forceinline__ void rope_row_regs(uint8_t* tile, int r, const float (&cr)[D / 2],
+                                              const float (&sr)[D / 2], uint32_t qcol) {
+  static_assert(D % 16 == 0, "whole 8-element chunks");
+  constexpr int NP = D / 16;
+#pragma unroll
+  for (int c = 0; c < NP; ++c) {
+    const uint4 ua = *reinterpret_cast<const uint4*>(tile + chunk_off(r, c));
+    const uint4 ub = *reinterpret_cast<const uint4*>(tile + chunk_off(r, c + NP));
+    float x0[8], x1[8];
+    unpack8<TI>(ua, x0);
+    unpack8<TI>(ub, x1);
+    uint4 oa, ob;
+    uint32_t* wa = reinterpret_cast<uint32_t*>(&oa);
+    uint32_t* wb = reinterpret_cast<uint32_t*>(&ob);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const int i = 8 * c + e;
+      wa[e / 2] = pack2<TI>(x0[e] * cr[i] - x1[e] * sr[i], x0[e + 1] * cr[i + 1] - x1[e + 1] * sr[i + 1]);
+      wb[e / 2] = pack2<TI>(x0[e] * sr[i] + x1[e] * cr[i], x0[e + 1] * sr[i + 1] + x1[e + 1] * cr[i + 1]);
+    }
+    if constexpr (TO_TMEM) {
+      tmem_st4(qcol + 4 * c, oa);
+      tmem_st4(qcol + 4 * (c + NP), ob);
+    } else {
+      *reinterpret_cast<uint4*>(tile + chunk_off(r, c)) = oa;
+      *reinterpret_cast<uint4*>(tile + chunk_off(r, c + NP)) = ob;
+    }
+  }
+}
+
+template <int D, typename TI, typename TC>
+__global__ void __launch_bounds__(kWinThreads, 2) window_attn_kernel(const __grid_constant__ Params p) {
+  using C = Cfg<D, static_cast<int>(sizeof(TC))>;
+  using W = WinCfg<D, static_cast<int>(sizeof(TC))>;
+  constexpr bool kBF16 = std::is_same<TI, __nv_bfloat16>::value;
+  constexpr uint32_t IDESC_S = make_idesc_f16(kBF16, kTileM, kTileN, false);
+  constexpr uint32_t IDESC_O = make_idesc_f16(kBF16, kTileM, C::DP, true);
+  constexpr uint32_t SW32 = 6;
+  constexpr int MODE = kRopeTable;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + W::OFF_BAR;
+  auto bar = [&](int i) -> uint32_t { return bar0 + 8u * static_cast<uint32_t>(i); };
+  Ctl* ctl = reinterpret_cast<Ctl*>(smem + W::OFF_BAR + 8 * W::COUNT);
+  volatile int* abort_flag = &ctl->abort;
+  __shared__ int s_unit[6];        // kv0, kv1, first row, end row, staged cu entries, their first index
+  __shared__ int s_cu[kWinStage];  // cu_seqlens, or cu_seqlens[sa .. se + 1] when long
+
+  const int t = threadIdx.x;  // q row within the chunk == TMEM lane
+  const int warp = t >> 5;
+  const int lane = t & 31;
+  const int h = blockIdx.x;
+  const int q0 = blockIdx.y * kTileM;
+  const int q1 = min(q0 + kTileM, p.T);
+#ifdef FRATTN_TRACE
+  // per-CTA global-timer stamps: [cta][event], events 0 entry, 1 unit known,
+  // 2 Q rotated, 3 K arrived, 4 S ready, 5 P stored, 6 O ready, 7 exit
+  const int tr_cta = blockIdx.y * gridDim.x + blockIdx.x;
+#define WIN_TRACE(ev) \
+  do { if (tr_cta < kTraceWords / 8) g_trace[tr_cta * 8 + (ev)] = globaltimer_ns(); } while (0)
+#else
+#define WIN_TRACE(ev) do { } while (0)
+#endif
+  if (t == 0) WIN_TRACE(0);
+
+  // cos/sin of this thread's q row straight into registers (reused for its K
+  // row when the K tile is the chunk itself, as for windows that do not cross
+  // a chunk boundary); issued first so that the latency overlaps the rest.
+  constexpr int RD = D / 2;
+  float cr[RD], sr[RD];
+  {
+    const int rr = min(q0 + t, p.T - 1);
+    const TC* cp = static_cast<const TC*>(p.cos) + static_cast<size_t>(rr) * RD;
+    const TC* sp = static_cast<const TC*>(p.sin) + static_cast<size_t>(rr) * RD;
+    if constexpr (RD % 8 == 0) {
+#pragma unroll
+      for (int i = 0; i < RD; i += 8) {
+        float a[8], b[8];
+        load8<TC>(cp + i, a);
+        load8<TC>(sp + i, b);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          cr[i + e] = a[e];
+          sr[i + e] = b[e];
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < RD; ++i) {
+        cr[i] = to_f32<TC>(__ldg(cp + i));
+        sr[i] = to_f32<TC>(__ldg(sp + i));
+      }
+    }
+  }
+  const int n_all = p.nseg + 1;
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int i = 0; i < W::COUNT; ++i) mbar_init(bar(i), 1);
+      ctl->abort = 0;
+      fence_mbar_init();
+      fence_proxy_async_smem();
+      // Q does not depend on the segmentation: load first.
+      mbar_arrive_expect_tx(bar(W::Q_FULL), C::TILE_BYTES);
+#pragma unroll
+      for (int b = 0; b < C::KB; ++b)
+        tma_load_3d(sbase + W::OFF_Q + b * kBlkBytes, &p.tmq, bar(W::Q_FULL), 16 * b, h, q0);
+    }
+    __syncwarp();
+    tmem_alloc(smem_u32(&ctl->tmem_base), W::TMEM_COLS);
+    tmem_relinquish();
+  }
+  // cu_seqlens into shared memory in one round of loads when it is short (the
+  // usual case: a few hundred windows); a longer one is searched by warp 0.
+  if (n_all <= kWinStage)
+    for (int i = t; i < n_all; i += kWinThreads) s_cu[i] = __ldg(p.cu + i);
+  if (warp == 1 && blockIdx.x == 0 && blockIdx.y == 0) {
+    // cu_seqlens check (non-decreasing, inside [0, T]) by one warp per call.
+    int bad = 0;
+    for (int sg = lane; sg <= p.nseg; sg += 32) {
+      const int v0 = __ldg(p.cu + sg);
+      if (v0 < 0 || v0 > p.T) bad = 1;
+      if (sg < p.nseg && __ldg(p.cu + sg + 1) < v0) bad = 1;
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0 && p.status)
+      atomicCAS(reinterpret_cast<int*>(p.status), 0, FRATTN_STATUS_BAD_SEQLENS);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // Segments of this chunk: [sa, se] contain rows [a, e) = [q0, q1) clipped
+    // to [cu[0], cu[nseg]); kv rows [cu[sa], cu[se + 1]). Values are clamped
+    // to [0, T] so that a malformed cu_seqlens (reported above) cannot send a
+    // load or store out of bounds.
+    const bool small = n_all <= kWinStage;
+    auto cu_at = [&](int i) -> int { return small ? s_cu[i] : __ldg(p.cu + i); };
+    const int cu_first = min(max(cu_at(0), 0), p.T);
+    const int cu_last = min(max(cu_at(p.nseg), 0), p.T);
+    const int a = max(q0, cu_first), e = min(q1, cu_last);
+    int kv0 = 0, kv1 = 0, sa = 0, se = -1;
+    if (a < e) {
+      if (small) {
+        sa = upper_bound_smem(s_cu, n_all, a) - 1;
+        se = upper_bound_smem(s_cu, n_all, e - 1) - 1;
+      } else {
+        sa = warp_upper_bound(p.cu, n_all, a, lane) - 1;
+        se = warp_upper_bound(p.cu, n_all, e - 1, lane) - 1;
+      }
+      sa = min(max(sa, 0), p.nseg - 1);
+      se = min(max(se, sa), p.nseg - 1);
+      kv0 = min(max(cu_at(sa), 0), p.T);
+      kv1 = min(max(cu_at(se + 1), 0), p.T);
+      if (kv1 < kv0) kv1 = kv0;
+    }
+    const int n_stage = se - sa + 2;  // entries cu[sa .. se + 1]
+    if (lane == 0) {
+      s_unit[0] = kv0;
+      s_unit[1] = kv1;
+      s_unit[2] = a;
+      s_unit[3] = e;
+      // staged entries for the row lookups: all of cu (base 0) or this chunk's
+      s_unit[4] = a < e ? (small ? n_all : (n_stage <= kWinStage ? n_stage : 0)) : 0;
+      s_unit[5] = small ? 0 : sa;
+      if (kv1 > kv0) {  // first K/V tile right away
+        mbar_arrive_expect_tx(bar(W::K_FULL), C::TILE_BYTES);
+#pragma unroll
+        for (int b = 0; b < C::KB; ++b)
+          tma_load_3d(sbase + W::OFF_K + b * kBlkBytes, &p.tmk, bar(W::K_FULL), 16 * b, h, kv0);
+        mbar_arrive_expect_tx(bar(W::V_FULL), C::TILE_BYTES);
+#pragma unroll
+        for (int b = 0; b < C::KB; ++b)
+          tma_load_3d(sbase + W::OFF_V + b * kBlkBytes, &p.tmv, bar(W::V_FULL), 16 * b, h, kv0);
+      }
+    }
+    __syncwarp();
+    if (!small && a < e && n_stage <= kWinStage)
+      for (int i = lane; i < n_stage; i += 32) s_cu[i] = __ldg(p.cu + sa + i);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  const int kv0 = s_unit[0], kv1 = s_unit[1], ra = s_unit[2], re = s_unit[3], n_cu = s_unit[4];
+  const int cu_base = s_unit[5];
+  const int nkv = (kv1 - kv0 + kTileN - 1) / kTileN;
+  if (t == 0) WIN_TRACE(1);
+
+  const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  const uint32_t s_addr = lane_addr + W::TMEM_S;
+  const uint32_t o_addr = lane_addr + W::TMEM_O;
+  const int row = q0 + t;
+  int lo = 0, hi = 0;  // kv rows this q row attends to
+  if (row >= ra && row < re) {
+    if (n_cu > 0) {  // staged entries cu[cu_base .. cu_base + n_cu)
+      const int i = min(max(upper_bound_smem(s_cu, n_cu, row), 1), n_cu - 1);
+      lo = max(s_cu[i - 1], kv0);
+      hi = min(s_cu[i], kv1);
+      (void)cu_base;
+    } else {
+      const int sg = upper_bound_cu(p.cu, 0, p.nseg + 1, row) - 1;
+      lo = max(__ldg(p.cu + sg), kv0);
+      hi = min(__ldg(p.cu + sg + 1), kv1);
+    }
+  }
+  bool ok = true;
+  float m_ref = -INFINITY, l = 0.f;
+  if (nkv > 0) {
+    // rotated Q of row t into TMEM (A operand of S)
+    ok = bounded_wait_warp(bar(W::Q_FULL), 0, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x58);
+    if (ok) {
+      rope_row_regs<D, TI, true>(smem + W::OFF_Q, t, cr, sr, lane_addr + W::TMEM_Q);
+      tmem_st_wait();
+    }
+    if (t == 0) WIN_TRACE(2);
+    // K tile 0: rotated before the tile loop, with the register cos/sin when the
+    // tile is this chunk (they are dead afterwards).
+    ok = ok && bounded_wait_warp(bar(W::K_FULL), 0, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x59);
+    if (ok) {
+      if (t == 0) WIN_TRACE(3);
+      if (kv0 == q0)
+        rope_row_regs<D, TI, false>(smem + W::OFF_K, t, cr, sr, 0);
+      else
+        rope_tile<D, MODE, TI, TC>(smem + W::OFF_K, kv0, p, t, nullptr);
+      fence_proxy_async_smem();
+    }
+    const float sl2 = 1.4426950408889634f * rsqrtf(static_cast<float>(D));
+    constexpr float kRescaleLog2 = 8.0f;
+    for (int j = 0; j < nkv; ++j) {
+      const int krow = kv0 + j * kTileN;
+      if (j > 0 && t == 0) {  // next K/V tile once PV(j-1) has released the buffers
+        ok = bounded_wait(bar(W::KV_EMPTY), (j - 1) & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x51);
+        if (ok) {
+          mbar_arrive_expect_tx(bar(W::K_FULL), C::TILE_BYTES);
+#pragma unroll
+          for (int b = 0; b < C::KB; ++b)
+            tma_load_3d(sbase + W::OFF_K + b * kBlkBytes, &p.tmk, bar(W::K_FULL), 16 * b, h, krow);
+          mbar_arrive_expect_tx(bar(W::V_FULL), C::TILE_BYTES);
+#pragma unroll
+          for (int b = 0; b < C::KB; ++b)
+            tma_load_3d(sbase + W::OFF_V + b * kBlkBytes, &p.tmv, bar(W::V_FULL), 16 * b, h, krow);
+        }
+      }
+      // rotated K row t (in place, shared memory); tile 0 was rotated above
+      if (j > 0) {
+        ok = ok && bounded_wait_warp(bar(W::K_FULL), j & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x59);
+        if (ok) {
+          rope_tile<D, MODE, TI, TC>(smem + W::OFF_K, krow, p, t, nullptr);
+          fence_proxy_async_smem();
+        }
+      }
+      tc_fence_before();
+      ok = __syncthreads_and(ok);
+      tc_fence_after();
+      if (!ok) break;
+      if (t == 0) {  // S = Q K^T (Q from TMEM)
+        const uint64_t kdesc = make_sdesc(sbase + W::OFF_K, 16, 256, SW32);
+#pragma unroll
+        for (int kb = 0; kb < C::KB; ++kb)
+          umma_ts(tmem + W::TMEM_S, tmem + W::TMEM_Q + kb * 8,
+                  kdesc + static_cast<uint64_t>((kb * kBlkBytes) >> 4), IDESC_S, kb > 0 ? 1u : 0u);
+        umma_commit(bar(W::S_FULL));
+      }
+      ok = bounded_wait_warp(bar(W::S_FULL), j & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x5A);
+      if (!ok) break;
+      if (t == 0 && j == 0) WIN_TRACE(4);
+      tc_fence_after();
+      const int lo_r = lo - krow, hi_r = hi - krow;
+      // 32-column chunks that no row of this warp attends to keep P = 0 and
+      // cost no exponentials (the other windows of the tile).
+      uint32_t live = 0;
+#pragma unroll
+      for (int c = 0; c < kTileN / 32; ++c)
+        if (__any_sync(0xffffffffu, lo_r < 32 * c + 32 && hi_r > 32 * c)) live |= 1u << c;
+      float s[kTileN];
+#pragma unroll
+      for (int c = 0; c < kTileN / 32; ++c) {
+        uint32_t rr[32];
+        if (live & (1u << c)) {
+          tmem_ld32(s_addr + c * 32, rr);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(rr[e]);
+        }
+      }
+      tmem_ld_wait();
+      float mxq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < kTileN / 32; ++c) {
+        if (!(live & (1u << c))) continue;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int i = c * 32 + e;
+          if (i < lo_r || i >= hi_r) s[i] = -INFINITY;
+        }
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            mxq[q] = max3(mxq[q], s[c * 32 + e + 2 * q], s[c * 32 + e + 2 * q + 1]);
+        }
+      }
+      const float mx = max3(fmaxf(mxq[0], mxq[1]), mxq[2], mxq[3]);
+      float alpha = 1.f;
+      bool rescale = false;
+      if (mx > m_ref && (m_ref == -INFINITY || (mx - m_ref) * sl2 > kRescaleLog2)) {
+        alpha = (m_ref == -INFINITY) ? 0.f : ex2((m_ref - mx) * sl2);
+        rescale = l > 0.f;
+        m_ref = mx;
+      }
+      const float mb = (m_ref == -INFINITY ? 0.f : m_ref) * sl2;
+      const uint64_t scale2 = f2pack(sl2, sl2);
+      const uint64_t bias2 = f2pack(-mb, -mb);
+      uint64_t sp2[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int c = 0; c < kTileN / 32; ++c) {
+        uint32_t pk[16];
+        if (live & (1u << c)) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const uint64_t xa = fma2(f2pack(s[c * 32 + 2 * e], s[c * 32 + 2 * e + 1]), scale2, bias2);
+            float a0, a1;
+            f2unpack(xa, a0, a1);
+            const uint64_t pp = f2pack(ex2(a0), ex2(a1));
+            sp2[e & 3] = add2(sp2[e & 3], pp);
+            float p0, p1;
+            f2unpack(pp, p0, p1);
+            pk[e] = pack2<TI>(p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) pk[e] = 0u;
+        }
+        tmem_st16(s_addr + c * 16, pk);
+      }
+      float sa_, sb_, sc_, sd_;
+      f2unpack(add2(sp2[0], sp2[1]), sa_, sb_);
+      f2unpack(add2(sp2[2], sp2[3]), sc_, sd_);
+      l = l * alpha + ((sa_ + sb_) + (sc_ + sd_));
+      // O holds PV(j-1) complete: S(j) was issued after it by the same thread.
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+        for (int c = 0; c < C::DP / 16; ++c) {
+          uint32_t rr[16];
+          tmem_ld16(o_addr + c * 16, rr);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
+          tmem_st16(o_addr + c * 16, rr);
+        }
+      }
+      if (t == 0 && j == 0) WIN_TRACE(5);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncthreads();
+      tc_fence_after();
+      if (t == 0) {  // O += P V (P from TMEM, where it overwrote S)
+        ok = bounded_wait(bar(W::V_FULL), j & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x54);
+        if (ok) {
+          const uint64_t vdesc = make_sdesc(sbase + W::OFF_V, kBlkBytes, 256, SW32);
+#pragma unroll
+          for (int kk = 0; kk < kTileN / 16; ++kk)
+            umma_ts(tmem + W::TMEM_O, tmem + W::TMEM_S + kk * 8,
+                    vdesc + static_cast<uint64_t>((kk * 512) >> 4), IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(bar(W::KV_EMPTY));
+          if (j == nkv - 1) umma_commit(bar(W::O_FULL));
+        }
+      }
+    }
+    ok = __syncthreads_and(ok);
+    if (ok) ok = bounded_wait_warp(bar(W::O_FULL), 0, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x5B);
+    if (t == 0) WIN_TRACE(6);
+    tc_fence_after();
+  }
+  // Epilogue: normalise and store the row; rows outside every segment are 0.
+  // (The TMEM loads are warp-wide; only the stores depend on the row.)
+  {
+    TI* orow = static_cast<TI*>(p.out) + (static_cast<size_t>(min(row, p.T - 1)) * p.H + h) * D;
+    const bool has = ok && lo < hi && l > 0.f;
+    const float inv_l = has ? 1.f / l : 0.f;
+    uint32_t oo[C::DP / 16][16];
+    if (nkv > 0) {
+#pragma unroll
+      for (int c = 0; c < C::DP / 16; ++c) tmem_ld16(o_addr + c * 16, oo[c]);
+      tmem_ld_wait();
+    }
+#pragma unroll
+    for (int c = 0; c < C::DP / 16; ++c) {
+      const uint32_t (&rr)[16] = oo[c];
+      uint4 w0, w1;
+      w0.x = pack2<TI>(has ? __uint_as_float(rr[0]) * inv_l : 0.f, has ? __uint_as_float(rr[1]) * inv_l : 0.f);
+      w0.y = pack2<TI>(has ? __uint_as_float(rr[2]) * inv_l : 0.f, has ? __uint_as_float(rr[3]) * inv_l : 0.f);
+      w0.z = pack2<TI>(has ? __uint_as_float(rr[4]) * inv_l : 0.f, has ? __uint_as_float(rr[5]) * inv_l : 0.f);
+      w0.w = pack2<TI>(has ? __uint_as_float(rr[6]) * inv_l : 0.f, has ? __uint_as_float(rr[7]) * inv_l : 0.f);
+      w1.x = pack2<TI>(has ? __uint_as_float(rr[8]) * inv_l : 0.f, has ? __uint_as_float(rr[9]) * inv_l : 0.f);
+      w1.y = pack2<TI>(has ? __uint_as_float(rr[10]) * inv_l : 0.f, has ? __uint_as_float(rr[11]) * inv_l : 0.f);
+      w1.z = pack2<TI>(has ? __uint_as_float(rr[12]) * inv_l : 0.f, has ? __uint_as_float(rr[13]) * inv_l : 0.f);
+      w1.w = pack2<TI>(has ? __uint_as_float(rr[14]) * inv_l : 0.f, has ? __uint_as_float(rr[15]) * inv_l : 0.f);
+      if (row < q1) {
+        if (c * 16 < D) reinterpret_cast<uint4*>(orow + c * 16)[0] = w0;
+        if (c * 16 + 8 < D) reinterpret_cast<uint4*>(orow + c * 16)[1] = w1;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, W::TMEM_COLS);
+  }
+  if (t == 0) WIN_TRACE(7);
+#undef WIN_TRACE
+}
+
+// Launch of the window kernel; FRATTN_E_SHAPE when this head dim has none
+// (the caller then uses the general path).
+template <int D, typename TI, typename TC>
+int launch_window(const Params& prm, cudaStream_t st) {
+  if constexpr (!(Cfg<D, static_cast<int>(sizeof(TC))>::Q_TMEM)) {
+    return FRATTN_E_SHAPE;
+  } else {
+    using W = WinCfg<D, static_cast<int>(sizeof(TC))>;
+    auto kern = window_attn_kernel<D, TI, TC>;
+    static unsigned long long attr_set = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (!(attr_set & bit)) {
+      // two CTAs per SM need the largest shared-memory carve-out
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, W::SMEM_BYTES) !=
+              cudaSuccess ||
+          cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) !=
+              cudaSuccess)
+        return FRATTN_E_CUDA;
+      attr_set |= bit;
+    }
+    const dim3 grid(prm.H, (prm.T + kTileM - 1) / kTileM);
+    kern<<<grid, kWinThreads, W::SMEM_BYTES, st>>>(prm);
+    return cudaGetLastError() == cudaSuccess ? 0 : FRATTN_E_CUDA;
+  }
+}
+
+template <int D, typename TI>
+int window_cs(const Params& prm, int cs_dtype, cudaStream_t st) {
+#ifdef FRATTN_FAST_BUILD
+  if (cs_dtype != FRATTN_F32) return FRATTN_E_SHAPE;
+  return launch_window<D, TI, float>(prm, st);
+#else
+  switch (cs_dtype) {
+    case FRATTN_F32: return launch_window<D, TI, float>(prm, st);
+    case FRATTN_BF16: return launch_window<D, TI, __nv_bfloat16>(prm, st);
+    case FRATTN_F16: return launch_window<D, TI, __half>(prm, st);
+    default: return FRATTN_E_DTYPE;
+  }
+#endif
+}
+
 }  // namespace frattn

@@ -19,7 +19,7 @@ import torch.distributed as dist
 
 from .encoder import EncoderConfig, encoder_flops, encoder_inputs
 
-__all__ = ["item_cost", "partition", "gather_packed", "run_dp"]
+__all__ = ["item_cost", "partition", "gather_packed", "local_inputs", "run_dp"]
 
 
 def item_cost(grid, cfg: EncoderConfig | None = None) -> float:
@@ -59,25 +59,45 @@ def gather_packed(x: torch.Tensor, group=None) -> list[torch.Tensor] | None:
     return [full[r * m: r * m + sizes[r]] for r in range(world)]
 
 
-def run_dp(encoder, grids, attn: str = "fused", seed: int = 0, group=None):
+def local_inputs(encoder, grids, parts, rank, seed: int = 0):
+    """This rank's packed input embeddings (item i seeded by seed + i) and its grids."""
+    cfg = encoder.cfg
+    mine = parts[rank]
+    dev, dt = encoder.device, encoder.dtype
+    if not mine:
+        return torch.zeros(0, cfg.hidden, device=dev, dtype=dt), []
+    xs = [encoder_inputs([grids[i]], cfg.hidden, seed=seed + i, device=dev, dtype=dt) for i in mine]
+    return torch.cat(xs), [grids[i] for i in mine]
+
+
+def run_dp(encoder, grids, attn: str = "fused", seed: int = 0, group=None, inputs=None, plan=None,
+           events=None):
     """One data-parallel encoder pass over ``grids`` (list of (t, h, w)).
 
     Every item's input embeddings are seeded by its index, so the result does
-    not depend on the partition. Returns (outputs on rank 0 else None, my item
-    indices, local token count).
+    not depend on the partition. ``inputs`` / ``plan`` may be prepared ahead
+    (``local_inputs``, ``encoder.plan``) so that a timed pass only runs the
+    encoder and the gather; ``events`` = three CUDA events recorded before the
+    encoder, between encoder and gather, and after the gather. Returns (outputs
+    on rank 0 else None, my item indices, local token count).
     """
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     cfg = encoder.cfg
     parts = partition([item_cost(g, cfg) for g in grids], world)
     mine = parts[rank]
-    dev, dt = encoder.device, encoder.dtype
+    x, my_grids = inputs if inputs is not None else local_inputs(encoder, grids, parts, rank, seed)
+    if events:
+        events[0].record()
     if mine:
-        xs = [encoder_inputs([grids[i]], cfg.hidden, seed=seed + i, device=dev, dtype=dt) for i in mine]
-        out = encoder(torch.cat(xs), [grids[i] for i in mine], attn=attn)
+        out = encoder(x, my_grids, attn=attn, plan=plan)
     else:
-        out = torch.zeros(0, cfg.hidden, device=dev, dtype=dt)
+        out = x
+    if events:
+        events[1].record()
     gathered = gather_packed(out, group)
+    if events:
+        events[2].record()
     if gathered is None:
         return None, mine, out.shape[0]
     result: list[torch.Tensor | None] = [None] * len(grids)

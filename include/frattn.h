@@ -158,6 +158,40 @@ int frattn_fwd_noalloc(const void* q, const void* k, const void* v, const void* 
                        int H, int D, int max_seqlen, int in_dtype, void* out, int32_t* status,
                        void* stream);
 
+/* ---- Window plan on the device (no host-side index arithmetic, no large
+ * host->device copies). Replaces the host producers of the kernel's inputs:
+ *   utils.py:12-102        get_window_index(grid_thw, window_size, merge, patch)
+ *   utils.py:105-153       window_shuffle / window_unshuffle
+ *   fused_attn.py:125-134  compute_rope_2d(..., window_idx=...) window-ordered tables
+ * grid_thw is a HOST array [num_images][3] of (t, h, w) patch counts (h, w
+ * divisible by merge). Windows are window_size / merge / patch_size merge units
+ * on a side, visited row-major per frame, units row-major inside a window, edge
+ * windows truncated (the reference's order; no window is ever empty).
+ *
+ * frattn_window_plan_sizes: number of merge units U (= T / merge^2), windows W
+ * and the device workspace the plan needs.
+ * frattn_window_plan writes (device pointers, stream-ordered):
+ *   window_index [U] int64  source merge unit of each window-order slot
+ *   cu_seqlens   [W + 1] int32 token offsets of the windows
+ *   pos_hw       [T, 2] int32 (h, w) patch position of each token in window
+ *                order, or NULL (input of frattn_fwd_pos)
+ *   cos_table, sin_table [T, rotary_dim] fp32 in window order, or both NULL:
+ *                index i < rotary_dim/2 uses h, the rest w, with
+ *                inv_freq[i] = theta^(-2i / rotary_dim) (rotary_dim = head_dim / 2)
+ * frattn_window_shuffle: rows of row_bytes (multiple of 16) bytes;
+ *   inverse = 0: out[p m2 + j] = x[window_index[p] m2 + j] (into window order),
+ *   inverse = 1: out[window_index[p] m2 + j] = x[p m2 + j] (back), m2 = merge^2.
+ *   x and out must not overlap. */
+int frattn_window_plan_sizes(const int32_t* grid_thw, int num_images, int window_size, int merge,
+                             int patch_size, int64_t* units, int64_t* windows,
+                             size_t* workspace_bytes);
+int frattn_window_plan(const int32_t* grid_thw, int num_images, int window_size, int merge,
+                       int patch_size, int64_t* window_index, int32_t* cu_seqlens, int32_t* pos_hw,
+                       float* cos_table, float* sin_table, int rotary_dim, float theta,
+                       void* workspace, size_t workspace_bytes, void* stream);
+int frattn_window_shuffle(const void* x, const int64_t* window_index, int64_t units, int merge_unit,
+                          int64_t row_bytes, int inverse, void* out, void* stream);
+
 /* Test hook for the bounded-wait failure path: launches one CTA that waits on
  * an mbarrier nothing ever arrives on, with a `limit_ns` bound, and returns
  * through *status (FRATTN_STATUS_WAIT_TIMEOUT | ...) without faulting or

@@ -51,10 +51,11 @@ def test_config_parity(name, grid, windowed):
     assert_close(run(*case), oracle(*case))
 
 
-def test_cfg3_mixed_varlen_batch():
+@pytest.mark.parametrize("hint", [None, 64])
+def test_cfg3_mixed_varlen_batch(hint):
     grid = [(1, s, s) for s in mixed_sides(0)]
     case = grid_case(grid, True, seed=3)
-    assert_close(run(*case), oracle(*case))
+    assert_close(run(*case, max_seqlen=hint), oracle(*case))
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
@@ -92,10 +93,16 @@ def test_padded_head_dims(D):
     [0, 5, 9, 70, 71, 200, 330, 331, 459],   # ragged, segments crossing 128-row chunks
     list(range(0, 1025, 1)),                 # 1024 length-1 segments
     [0, 3000],                               # one long segment, partial last tile
+    list(range(0, 2050, 2)),                 # 1024 two-token segments (cu longer than the staged part)
+    [0, 60, 64, 130, 131, 250, 300, 364],    # windows crossing 128-row chunks (two K/V tiles)
 ])
-def test_edge_segmentations(cu_list):
+@pytest.mark.parametrize("hint", [False, True], ids=["general", "max_seqlen_hint"])
+def test_edge_segmentations(cu_list, hint):
+    # With the hint (the longest segment, as callers pass it) segments of at
+    # most 128 tokens take the window kernel, longer ones the general path.
     case = cu_case(cu_list, H=2, seed=len(cu_list))
-    assert_close(run(*case), oracle(*case))
+    kw = {"max_seqlen": max(b - a for a, b in zip(cu_list[:-1], cu_list[1:]))} if hint else {}
+    assert_close(run(*case, **kw), oracle(*case))
 
 
 def test_rows_outside_segments_are_zero():
