@@ -32,6 +32,8 @@ _SIGNATURES = {
     "frattn_workspace_bytes_pos": (_i, [_i, _i, _i, _i, ctypes.POINTER(_sz)]),
     "frattn_workspace_bytes_rotated_k": (_i, [_i, _i, _i, ctypes.POINTER(_sz)]),
     "frattn_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _sz, _vp, _vp]),
+    "frattn_fwd_strided": (_i, [_vp, _vp, _vp, ctypes.c_longlong, ctypes.c_longlong, ctypes.c_longlong, _vp, _vp,
+                               _i, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _sz, _vp, _vp]),
     "frattn_fwd_pos": (_i, [_vp, _vp, _vp, _vp, _i, _f, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _sz, _vp, _vp]),
     "frattn_fwd_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
     "frattn_window_plan_sizes": (_i, [_vp, _i, _i, _i, _i, ctypes.POINTER(ctypes.c_int64),

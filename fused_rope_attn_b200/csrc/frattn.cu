@@ -69,12 +69,13 @@ PFN_encodeTiled get_encode_fn() {
 unsigned long long g_wait_limit_ns = 2000000000ull;
 
 // [T, H, D] tensor viewed as 3-D {D, H, T}; box {16, 1, 128}, 32-B swizzle.
-int make_qkv_map(CUtensorMap* m, const void* base, int T, int H, int D, bool bf16) {
+int make_qkv_map(CUtensorMap* m, const void* base, int T, int H, int D, bool bf16,
+                 long long row_stride) {
   PFN_encodeTiled enc = get_encode_fn();
   if (!enc) return FRATTN_E_TMAP;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(H),
                         static_cast<cuuint64_t>(T)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(H) * D * 2};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(row_stride) * 2};
   cuuint32_t box[3] = {16, 1, static_cast<cuuint32_t>(kTileM)};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
@@ -183,9 +184,18 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
              int cs_dtype, const int32_t* pos_hw, int max_position, float theta,
              const int32_t* cu, int nseg, int T, int H, int D, int in_dtype, void* out,
              void* workspace, size_t ws_bytes, int32_t* status, void* stream,
-             int max_seqlen = 0) {
+             int max_seqlen = 0, long long q_stride = 0, long long k_stride = 0,
+             long long v_stride = 0) {
   int rc = common_checks(q, k, v, cu, nseg, T, H, D, in_dtype, out, workspace);
   if (rc) return rc;
+  // token strides of q, k, v in elements (0: contiguous [T, H, D]); TMA needs
+  // every row start 16-byte aligned
+  const long long hd = static_cast<long long>(H) * D;
+  if (q_stride == 0) q_stride = hd;
+  if (k_stride == 0) k_stride = hd;
+  if (v_stride == 0) v_stride = hd;
+  if (q_stride < hd || k_stride < hd || v_stride < hd) return FRATTN_E_SHAPE;
+  if ((q_stride | k_stride | v_stride) & 7) return FRATTN_E_ALIGN;
   size_t need = 0;
   if (MODE == kRopeTable) {
     frattn_workspace_bytes(T, nseg, &need);
@@ -218,8 +228,9 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
   Params prm;
   memset(&prm, 0, sizeof(prm));
   const bool bf16 = in_dtype == FRATTN_BF16;
-  if (make_qkv_map(&prm.tmq, q, T, H, D, bf16) || make_qkv_map(&prm.tmk, k, T, H, D, bf16) ||
-      make_qkv_map(&prm.tmv, v, T, H, D, bf16))
+  if (make_qkv_map(&prm.tmq, q, T, H, D, bf16, q_stride) ||
+      make_qkv_map(&prm.tmk, k, T, H, D, bf16, k_stride) ||
+      make_qkv_map(&prm.tmv, v, T, H, D, bf16, v_stride))
     return FRATTN_E_TMAP;
   // Rotated-K buffer after the work list (and table) when the workspace has
   // room. A caller's max_seqlen <= one tile says no segment is long, so the
@@ -231,7 +242,8 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
   const bool no_long = max_seqlen > 0 && max_seqlen <= kTileM;
   if (ws_bytes >= krot_off + krot_bytes && !no_long) {
     prm.krot = ws + krot_off;
-    if (make_qkv_map(&prm.tmk_rot, prm.krot, T, H, D, bf16)) return FRATTN_E_TMAP;
+    if (make_qkv_map(&prm.tmk_rot, prm.krot, T, H, D, bf16, static_cast<long long>(H) * D))
+      return FRATTN_E_TMAP;
   }
   // cos/sin rows are staged through TMA only when a row is a multiple of 16 bytes
   // (the kernel's Cfg::CS_BYTES makes the same decision).
@@ -240,6 +252,7 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
       (make_cs_map(&prm.tmcos, cos, T, D, cs_dtype) || make_cs_map(&prm.tmsin, sin, T, D, cs_dtype)))
     return FRATTN_E_TMAP;
   prm.k = k;
+  prm.k_stride = k_stride;
   prm.cos = cos;
   prm.sin = sin;
   prm.pos_hw = pos_hw;
@@ -352,6 +365,17 @@ int frattn_fwd(const void* q, const void* k, const void* v, const void* cos, con
   return fwd_impl<kRopeTable>(q, k, v, cos, sin, cs_dtype, nullptr, 0, 0.f, cu_seqlens, nseg, T,
                               H, D, in_dtype, out, workspace, workspace_bytes, status, stream,
                               max_seqlen);
+}
+
+int frattn_fwd_strided(const void* q, const void* k, const void* v, long long q_stride,
+                       long long k_stride, long long v_stride, const void* cos, const void* sin,
+                       int cs_dtype, const int32_t* cu_seqlens, int nseg, int T, int H, int D,
+                       int max_seqlen, int in_dtype, void* out, void* workspace,
+                       size_t workspace_bytes, int32_t* status, void* stream) {
+  if (q_stride <= 0 || k_stride <= 0 || v_stride <= 0) return FRATTN_E_SHAPE;
+  return fwd_impl<kRopeTable>(q, k, v, cos, sin, cs_dtype, nullptr, 0, 0.f, cu_seqlens, nseg, T,
+                              H, D, in_dtype, out, workspace, workspace_bytes, status, stream,
+                              max_seqlen, q_stride, k_stride, v_stride);
 }
 
 int frattn_fwd_pos(const void* q, const void* k, const void* v, const int32_t* pos_hw,

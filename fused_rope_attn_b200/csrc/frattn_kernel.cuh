@@ -109,7 +109,8 @@ struct Params {
   CUtensorMap tmq, tmk, tmv;
   CUtensorMap tmk_rot;
   CUtensorMap tmcos, tmsin; // [T, D/2] cos/sin tables, box {D/2, 128} (table mode)      // rotated K in the workspace (long segments), when krot != nullptr
-  const void* k;            // [T, H, D] raw K
+  const void* k;            // [T, H, D] raw K (token stride k_stride elements)
+  long long k_stride;
   void* krot;               // [T, H, D] K rotated once, rows of long segments only
   const void* cos;          // [T, D/2] (table mode)
   const void* sin;
@@ -542,10 +543,11 @@ __global__ void __launch_bounds__(256) rotate_k_long(const __grid_constant__ Par
     const int h = rem % p.H;
     const int row = __ldcg(&p.items[i].q0) + rem / p.H;
     if (row >= __ldcg(&p.items[i].q1)) continue;
-    const size_t base = (static_cast<size_t>(row) * p.H + h) * D;
+    const size_t base = (static_cast<size_t>(row) * p.H + h) * D;  // rotated copy: contiguous
+    const size_t ibase = static_cast<size_t>(row) * p.k_stride + static_cast<size_t>(h) * D;
     if constexpr (D % 16 != 0) {
       for (int j = 0; j < D / 2; ++j) {
-        const float x0 = to_f32<TI>(kin[base + j]), x1 = to_f32<TI>(kin[base + D / 2 + j]);
+        const float x0 = to_f32<TI>(kin[ibase + j]), x1 = to_f32<TI>(kin[ibase + D / 2 + j]);
         float c, sn;
         rope_coeff1<D, MODE, TC>(p, row, j, static_cast<const TC*>(nullptr), c, sn);
         kout[base + j] = from_f32<TI>(x0 * c - x1 * sn);
@@ -556,8 +558,8 @@ __global__ void __launch_bounds__(256) rotate_k_long(const __grid_constant__ Par
     uint4 ua[NP], ub[NP];
 #pragma unroll
     for (int c = 0; c < NP; ++c) {
-      ua[c] = __ldg(reinterpret_cast<const uint4*>(kin + base + 8 * c));
-      ub[c] = __ldg(reinterpret_cast<const uint4*>(kin + base + D / 2 + 8 * c));
+      ua[c] = __ldg(reinterpret_cast<const uint4*>(kin + ibase + 8 * c));
+      ub[c] = __ldg(reinterpret_cast<const uint4*>(kin + ibase + D / 2 + 8 * c));
     }
 #pragma unroll
     for (int c = 0; c < NP; ++c) {

@@ -127,6 +127,15 @@ class VisionEncoder(torch.nn.Module):
             return torch.nn.Parameter((torch.randn(*shape, generator=g) * cfg.init_std).to(device=device, dtype=dtype),
                                       requires_grad=False)
 
+        # The MLP width is stored padded to a multiple of 8 with zero rows /
+        # columns: silu(0) * 0 = 0 adds nothing, so the function is the
+        # cfg.mlp-wide one, while every GEMM operand row is 16-byte aligned
+        # (3420 x 2 B is not, and cuBLAS then falls back to sm80 kernels).
+        mlp_p = -(-mlp // 8) * 8
+
+        def pad_rows(t):
+            return torch.nn.functional.pad(t, (0, 0, 0, mlp_p - mlp)) if mlp_p != mlp else t
+
         self.layers = []
         for i in range(cfg.depth):
             layer = {
@@ -134,14 +143,18 @@ class VisionEncoder(torch.nn.Module):
                 "n2": torch.ones(hid, device=device, dtype=dtype),
                 "qkv_w": w(3 * hid, hid), "qkv_b": w(3 * hid),
                 "proj_w": w(hid, hid), "proj_b": w(hid),
-                "gate_w": w(mlp, hid), "up_w": w(mlp, hid), "down_w": w(hid, mlp),
             }
+            gate, up, down = w(mlp, hid), w(mlp, hid), w(hid, mlp)  # same draw order as unpadded
+            layer.update({
+                "gate_w": pad_rows(gate.data), "up_w": pad_rows(up.data),
+                "down_w": torch.nn.functional.pad(down.data, (0, mlp_p - mlp)) if mlp_p != mlp else down.data,
+            })
             self.layers.append(layer)
         self.device, self.dtype = torch.device(device), dtype
 
     def _rms(self, x, weight):
-        xf = x.float()
-        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.cfg.eps)).to(x.dtype) * weight
+        # torch's fused RMSNorm (fp32 statistics, one pass over x)
+        return torch.nn.functional.rms_norm(x, (x.shape[-1],), weight, self.cfg.eps)
 
     def plan(self, grid_thw):
         """Window permutation, cu_seqlens of both layer kinds and window-ordered cos/sin."""
@@ -175,8 +188,7 @@ class VisionEncoder(torch.nn.Module):
             if attn == "fused":
                 o = fused_rope_attention(q, k, v, plan["cos"], plan["sin"], cu, max_seqlen=max_len)
             elif attn == "unfused":
-                o = _attn_unfused(q.contiguous(), k.contiguous(), v.contiguous(), plan["cos"], plan["sin"], cu,
-                                  max_len)
+                o = _attn_unfused(q, k, v, plan["cos"], plan["sin"], cu, max_len)
             elif attn == "fp32":
                 o = _attn_fp32(q, k, v, plan["cos"], plan["sin"], cu)
             else:

@@ -180,6 +180,20 @@ def _aligned(t: torch.Tensor) -> torch.Tensor:
     return t if t.data_ptr() % 16 == 0 else t.clone()
 
 
+def _token_rows(t: torch.Tensor) -> tuple[torch.Tensor, int]:
+    """``t`` [T, H, D] as rows the kernel reads in place: (tensor, token stride in
+    elements). Views whose heads and dims are packed but whose tokens are spread
+    out (q/k/v of one fused QKV projection) are passed as they are; anything
+    else is copied to a contiguous tensor (as the reference does for every
+    non-contiguous input, fused_attn.py:187-193)."""
+    T, H, D = t.shape
+    if (t.stride(2) == 1 and t.stride(1) == D and t.stride(0) >= H * D and t.stride(0) % 8 == 0
+            and t.data_ptr() % 16 == 0):
+        return t, int(t.stride(0))
+    t = _aligned(t.contiguous())
+    return t, H * D
+
+
 def _check_qkv(q, k, v):
     if q.device.type != "cuda":
         raise ValueError(f"q must be on CUDA, got device={q.device}")
@@ -303,7 +317,7 @@ def fused_rope_attention(
             return res.contiguous()
         out.copy_(res)
         return out
-    q, k, v = (_aligned(t.contiguous()) for t in (q, k, v))
+    (q, qs), (k, ks), (v, vs) = (_token_rows(t) for t in (q, k, v))
     cos = _aligned(cos.to(q.device).contiguous())
     sin = _aligned(sin.to(q.device).contiguous())
     out = _check_out(out, q)
@@ -316,11 +330,18 @@ def fused_rope_attention(
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream
-        rc = lib.frattn_fwd(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), cos.data_ptr(), sin.data_ptr(), _DT[cos.dtype],
-            cu.data_ptr(), nseg, total, heads, hd, int(max_seqlen or 0), _DT[q.dtype],
-            out.data_ptr(), ws.data_ptr(), ws_bytes, _status_word(q.device).data_ptr(), stream,
-        )
+        if qs == ks == vs == heads * hd:
+            rc = lib.frattn_fwd(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), cos.data_ptr(), sin.data_ptr(), _DT[cos.dtype],
+                cu.data_ptr(), nseg, total, heads, hd, int(max_seqlen or 0), _DT[q.dtype],
+                out.data_ptr(), ws.data_ptr(), ws_bytes, _status_word(q.device).data_ptr(), stream,
+            )
+        else:
+            rc = lib.frattn_fwd_strided(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), qs, ks, vs, cos.data_ptr(), sin.data_ptr(),
+                _DT[cos.dtype], cu.data_ptr(), nseg, total, heads, hd, int(max_seqlen or 0), _DT[q.dtype],
+                out.data_ptr(), ws.data_ptr(), ws_bytes, _status_word(q.device).data_ptr(), stream,
+            )
     _lib.check(rc, "frattn_fwd")
     return out
 

@@ -106,6 +106,19 @@ int frattn_fwd(const void* q, const void* k, const void* v, const void* cos, con
                int max_seqlen, int in_dtype, void* out, void* workspace, size_t workspace_bytes,
                int32_t* status, void* stream);
 
+/* frattn_fwd for q, k, v whose token rows are spread out: element (t, h, d)
+ * of q is q[t * q_stride + h * D + d] (likewise k, v), e.g. the three views
+ * of one fused [T, 3, H, D] QKV projection output (strides 3 H D). Strides are
+ * in elements, at least H * D and multiples of 8 (16-byte row starts, a TMA
+ * requirement; FRATTN_E_ALIGN otherwise). The reference copies such inputs to
+ * contiguous tensors first (fused_attn.py:187-193); here the tensor maps read
+ * them in place. out stays contiguous [T, H, D]. */
+int frattn_fwd_strided(const void* q, const void* k, const void* v, long long q_stride,
+                       long long k_stride, long long v_stride, const void* cos, const void* sin,
+                       int cs_dtype, const int32_t* cu_seqlens, int nseg, int T, int H, int D,
+                       int max_seqlen, int in_dtype, void* out, void* workspace,
+                       size_t workspace_bytes, int32_t* status, void* stream);
+
 /* Same operation with the 2D rotary angles generated in the kernel from integer
  * (h, w) patch positions instead of materialised cos/sin tables
  * (compute_rope_2d, fused_attn.py:77-116, without the dtype cast):

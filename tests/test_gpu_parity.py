@@ -105,6 +105,24 @@ def test_edge_segmentations(cu_list, hint):
     assert_close(run(*case, **kw), oracle(*case))
 
 
+@pytest.mark.parametrize("hint", [None, 64])
+def test_strided_qkv_views_match_contiguous(hint):
+    """q/k/v as views of one [T, 3, H, D] projection output (token stride 3 H D)
+    are read in place (frattn_fwd_strided) and give the contiguous result."""
+    grid = [(1, 22, 30), (1, 16, 16)]
+    q, k, v, cos, sin, cu = grid_case(grid, True, H=4, seed=13)
+    qkv = torch.stack([q, k, v], dim=1).to(DEV)  # [T, 3, H, D]
+    qv, kv_, vv = qkv[:, 0], qkv[:, 1], qkv[:, 2]
+    assert not qv.is_contiguous()
+    out = run(qv, kv_, vv, cos, sin, cu, max_seqlen=hint)
+    ref = run(q, k, v, cos, sin, cu, max_seqlen=hint)
+    assert torch.equal(out, ref)
+    assert_close(out, oracle(q, k, v, cos, sin, cu))
+    # a long segment through the same views (pre-rotated K path)
+    cu2 = torch.tensor([0, 300, int(cu[-1])], dtype=torch.int32)
+    assert torch.equal(run(qv, kv_, vv, cos, sin, cu2), run(q, k, v, cos, sin, cu2))
+
+
 def test_rows_outside_segments_are_zero():
     q, k, v, cos, sin, cu = cu_case([40, 104, 170], H=2, T=256, seed=9)
     out = run(q, k, v, cos, sin, cu).float().cpu()
