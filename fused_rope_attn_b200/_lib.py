@@ -42,6 +42,7 @@ _SIGNATURES = {
     "frattn_window_shuffle": (_i, [_vp, _vp, ctypes.c_int64, _i, ctypes.c_int64, _i, _vp, _vp]),
     "frattn_selftest_wait_timeout": (_i, [_vp, _u64, _vp]),
     "frattn_set_wait_limit_ns": (_i, [_u64]),
+    "frattn_set_timing_events": (_i, [_vp, _vp]),
 }
 
 _lib = None

@@ -212,6 +212,14 @@ int frattn_window_shuffle(const void* x, const int64_t* window_index, int64_t un
  * detection). */
 int frattn_selftest_wait_timeout(int32_t* status, uint64_t limit_ns, void* stream);
 
+/* Measurement hook (no counterpart in the reference): the next frattn_fwd /
+ * frattn_fwd_strided / frattn_fwd_pos call from this host thread records the
+ * two CUDA events (cudaEvent_t) on its stream around its attention kernels
+ * (the K pre-rotation and the attention kernel, or the window kernel), not
+ * around the work-list kernel. Recorded during stream capture they become
+ * event nodes of the graph. The events are forgotten after that call. */
+int frattn_set_timing_events(void* start_event, void* stop_event);
+
 /* Upper bound (nanoseconds) of every mbarrier wait inside the kernels;
  * default 2e9. A wait that exceeds it sets *status and the kernel returns. */
 int frattn_set_wait_limit_ns(uint64_t limit_ns);

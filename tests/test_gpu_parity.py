@@ -123,6 +123,30 @@ def test_strided_qkv_views_match_contiguous(hint):
     assert torch.equal(run(qv, kv_, vv, cos, sin, cu2), run(q, k, v, cos, sin, cu2))
 
 
+@pytest.mark.parametrize("cu_list,H,D,dtype", [
+    ([0, 3000, 5000], 16, 80, torch.bfloat16),       # 320 long units, two tile counts
+    ([0, 4096], 16, 80, torch.bfloat16),             # BASELINE config 2b shape: 256 units
+    ([0, 700, 2600, 2601, 4000], 24, 64, torch.float16),
+    ([0, 1500, 3100], 20, 128, torch.bfloat16),      # Q in shared memory (D = 128)
+])
+def test_long_units_split_across_ctas(cu_list, H, D, dtype):
+    """More long (segment, 256-row, head) units than CTAs: the long work is cut
+    into equal contiguous ranges per CTA and units cut at a range edge are
+    merged from fp32 partials (no rows of the oracle check are left out)."""
+    case = cu_case(cu_list, H=H, D=D, dtype=dtype, seed=H + D)
+    q, k, v, cos, sin, cu = case
+    out = run(*case)
+    rows = np.random.default_rng(1).choice(q.shape[0], 160, replace=False)
+    qr = O.apply_rope(q.float().numpy(), cos.numpy(), sin.numpy())
+    kr = O.apply_rope(k.float().numpy(), cos.numpy(), sin.numpy())
+    ref = O.varlen_attention_rows(qr, kr, v.float().numpy(), cu.numpy(), rows)
+    assert_close(out[rows.tolist()], ref)
+    # cross-check against the window kernel, which walks every chunk's whole kv
+    # range itself (a max_seqlen hint <= 128 selects it; results never depend
+    # on the hint)
+    assert (run(*case, max_seqlen=1).float() - out.float()).abs().max().item() <= 1e-2
+
+
 def test_rows_outside_segments_are_zero():
     q, k, v, cos, sin, cu = cu_case([40, 104, 170], H=2, T=256, seed=9)
     out = run(q, k, v, cos, sin, cu).float().cpu()
