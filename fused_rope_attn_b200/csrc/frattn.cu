@@ -15,7 +15,7 @@ namespace frattn {
   int window_d##DD(const Params& prm, int in_dtype, int cs_dtype, cudaStream_t st);            \
   int prep_d##DD(const int32_t* cu, int nseg, int T, int H, WorkItem* items, int* header,     \
                  void* out, int32_t* status, const int32_t* pos_hw, float* pos_tab,           \
-                 int pos_rows, float theta, int* split_cnt, int in_dtype, cudaStream_t st);
+                 int pos_rows, float theta, int in_dtype, cudaStream_t st);
 #ifdef FRATTN_FAST_BUILD
 FRATTN_DECL(80)
 #else
@@ -153,12 +153,12 @@ int dispatch_window(const Params& prm, int D, int in_dtype, int cs_dtype, cudaSt
 // Work-list kernel of head dimension D.
 int launch_prep(const int32_t* cu, int nseg, int T, int H, int D, WorkItem* items, int* header,
                 void* out, int32_t* status, const int32_t* pos_hw, float* pos_tab, int pos_rows,
-                float theta, int* split_cnt, int in_dtype, cudaStream_t st) {
+                float theta, int in_dtype, cudaStream_t st) {
   switch (D) {
 #define FRATTN_CASE(DD)                                                                       \
     case DD:                                                                                  \
       return prep_d##DD(cu, nseg, T, H, items, header, out, status, pos_hw, pos_tab, pos_rows, \
-                        theta, split_cnt, in_dtype, st);
+                        theta, in_dtype, st);
 #ifdef FRATTN_FAST_BUILD
     FRATTN_CASE(80)
 #else
@@ -175,12 +175,6 @@ bool supported_head_dim(int D) {
 #else
   return D % 8 == 0 && D >= 32 && D <= 128;
 #endif
-}
-
-// fp32 partial rows of split pieces: [CTA][first/last piece][slot][128 rows][DP + 4]
-size_t split_part_bytes(int ctas, int D) {
-  const size_t dp = (D + 15) / 16 * 16;
-  return (static_cast<size_t>(ctas) * 2 * 2 * kTileM * (dp + 4) * sizeof(float) + 255) & ~size_t(255);
 }
 
 size_t pos_table_bytes(int max_position, int D) {
@@ -243,7 +237,7 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
   }
   if (T == 0)
     return launch_prep(cu, nseg, T, H, D, items, header, out, status, pos_hw, pos_tab,
-                       max_position, theta, nullptr, in_dtype, st);
+                       max_position, theta, in_dtype, st);
 
   Params prm;
   memset(&prm, 0, sizeof(prm));
@@ -264,15 +258,6 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
     prm.krot = ws + krot_off;
     if (make_qkv_map(&prm.tmk_rot, prm.krot, T, H, D, bf16, static_cast<long long>(H) * D))
       return FRATTN_E_TMAP;
-    // Split pieces of long units (partials of at most two pieces per CTA):
-    // enabled when the rest of the rotated-K workspace holds them.
-    const size_t split_off = (krot_off + krot_bytes + 255) & ~size_t(255);
-    const size_t cnt_bytes = (max_items(T) * static_cast<size_t>(H) * 8 * sizeof(int) + 255) & ~size_t(255);
-    const size_t part_bytes = split_part_bytes(sm_count_for_current_device(), D);
-    if (ws_bytes >= split_off + cnt_bytes + part_bytes) {
-      prm.split_cnt = reinterpret_cast<int*>(ws + split_off);
-      prm.split_part = reinterpret_cast<float*>(ws + split_off + cnt_bytes);
-    }
   }
   // cos/sin rows are staged through TMA only when a row is a multiple of 16 bytes
   // (the kernel's Cfg::CS_BYTES makes the same decision).
@@ -308,7 +293,7 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
     }
   }
   rc = launch_prep(cu, nseg, T, H, D, items, header, out, status, pos_hw, pos_tab, max_position,
-                   theta, prm.split_cnt, in_dtype, st);
+                   theta, in_dtype, st);
   if (rc) return rc;
   timing_begin(st);  // around the K pre-rotation (if any) and the attention kernel
   rc = dispatch_head_dim(prm, MODE, D, in_dtype, cs_dtype, st);
@@ -379,11 +364,7 @@ int frattn_workspace_bytes_rotated_k(int total_tokens, int num_heads, int head_d
                                      size_t* bytes) {
   if (!bytes) return FRATTN_E_NULL;
   if (total_tokens < 0 || num_heads <= 0 || head_dim <= 0) return FRATTN_E_SHAPE;
-  // rotated K copy, then the split-piece counters and partial rows
-  const size_t krot = (static_cast<size_t>(total_tokens) * num_heads * head_dim * 2 + 255) & ~size_t(255);
-  const size_t cnt = (max_items(total_tokens) * static_cast<size_t>(num_heads) * 8 * sizeof(int) + 255) &
-                     ~size_t(255);
-  *bytes = 512 + krot + cnt + split_part_bytes(sm_count_for_current_device(), head_dim);
+  *bytes = 256 + static_cast<size_t>(total_tokens) * num_heads * head_dim * 2;
   return 0;
 }
 

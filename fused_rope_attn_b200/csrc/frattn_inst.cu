@@ -36,16 +36,16 @@ int FRATTN_CAT(window_d, FRATTN_D)(const Params& prm, int in_dtype, int cs_dtype
 // Work-list (scheduler) kernel of this head dimension.
 int FRATTN_CAT(prep_d, FRATTN_D)(const int32_t* cu, int nseg, int T, int H, WorkItem* items,
                                  int* header, void* out, int32_t* status, const int32_t* pos_hw,
-                                 float* pos_tab, int pos_rows, float theta, int* split_cnt,
-                                 int in_dtype, cudaStream_t st) {
+                                 float* pos_tab, int pos_rows, float theta, int in_dtype,
+                                 cudaStream_t st) {
   if (in_dtype == FRATTN_BF16)
     build_worklist<__nv_bfloat16, FRATTN_D><<<1, kPrepThreads, 0, st>>>(
         cu, nseg, T, H, items, header, static_cast<__nv_bfloat16*>(out), status, pos_hw, pos_tab,
-        pos_rows, theta, split_cnt);
+        pos_rows, theta);
   else
     build_worklist<__half, FRATTN_D><<<1, kPrepThreads, 0, st>>>(
         cu, nseg, T, H, items, header, static_cast<__half*>(out), status, pos_hw, pos_tab, pos_rows,
-        theta, split_cnt);
+        theta);
   return cudaGetLastError() == cudaSuccess ? 0 : FRATTN_E_CUDA;
 }
 

@@ -45,7 +45,6 @@
 #include <stdio.h>
 #include <string.h>
 
-#include <algorithm>
 #include <mutex>
 #include <type_traits>
 
@@ -126,18 +125,12 @@ struct Params {
   int T, H;
   int32_t* status;
   unsigned long long wait_limit_ns;
-  // Split pieces of long units (null: every unit runs whole on one CTA):
-  // per-(unit, slot) arrival counters and per-(CTA, first/last piece, slot)
-  // fp32 partial rows of PART_STRIDE floats (O, reference, row sum).
-  int* split_cnt;
-  float* split_part;
 };
 
 // ------------------------------------------------------------------ helpers
 struct Ctl {
   uint32_t tmem_base;
   int abort;
-  int bcast[2];  // per slot: counter value seen by the slot's first thread (split merge)
 };
 
 // Timeline trace (build with -DFRATTN_TRACE): SM clock stamps of pipeline
@@ -605,11 +598,6 @@ struct Unit {
   int ha, hb;
   int kv0, kv1, seg_lo, seg_hi, kind;
   bool has_b, shared;
-  // K/V tiles [jb, jb + nt) of the unit's kv range (all of them unless split)
-  int jb, nt;
-  bool split;     // a piece of a unit that other CTAs also work on
-  int uid;        // long unit index (split pieces)
-  int pkind;      // 0: the piece starts this CTA's range, 1: it ends it
 };
 
 __device__ __forceinline__ Unit decode_unit(const Params& p, int u, int n_long) {
@@ -642,82 +630,7 @@ __device__ __forceinline__ Unit decode_unit(const Params& p, int u, int n_long) 
   U.seg_lo = it.seg_lo;
   U.seg_hi = it.seg_hi;
   U.kind = it.kind;
-  U.jb = 0;
-  U.nt = (it.kv1 - it.kv0 + kTileN - 1) / kTileN;
-  U.split = false;
-  U.uid = u;
-  U.pkind = 0;
   return U;
-}
-
-// Work schedule of one CTA. Without split pieces: units blockIdx.x,
-// blockIdx.x + G, ... (G = gridDim.x). With them (more long units than CTAs):
-// the long work, W = sum over long units of their K/V tiles in unit order, is
-// cut into G equal contiguous ranges, CTA b taking [W b / G, W (b + 1) / G)
-// (a static stream-K partition: no CTA waits for the last wave), and the
-// packed units follow strided as before. A range edge that falls inside a
-// unit leaves a piece of it to each neighbouring CTA; those pieces are merged
-// by whichever finishes last (split_merge).
-struct Sched {
-  long long pos, end, W;
-  int pk, k;
-  bool split;
-};
-
-__device__ __forceinline__ long long range_start(long long W, int c, int G) {
-  return W * c / G;
-}
-// CTA whose range holds long-work position x.
-__device__ __forceinline__ int range_owner(long long W, long long x, int G) {
-  return static_cast<int>(min(static_cast<long long>(G - 1), ((x + 1) * G - 1) / W));
-}
-
-__device__ __forceinline__ void sched_init(const Params& p, Sched& sc, int n_long) {
-  const int G = static_cast<int>(gridDim.x), b = static_cast<int>(blockIdx.x);
-  sc.W = __ldcg(p.header + 2);
-  sc.split = p.split_cnt != nullptr && n_long * p.H > G && sc.W > 0;
-  sc.k = 0;
-  if (sc.split) {
-    sc.pos = range_start(sc.W, b, G);
-    sc.end = range_start(sc.W, b + 1, G);
-    sc.pk = n_long * p.H + b;
-  } else {
-    sc.pos = sc.end = 0;
-    sc.pk = b;
-  }
-}
-
-// Next unit or piece of this CTA (false when done).
-__device__ __forceinline__ bool sched_next(const Params& p, Sched& sc, int n_long, int n_units,
-                                           Unit& U) {
-  if (sc.split && sc.pos < sc.end) {
-    // long item holding position pos: items carry their first position in pad
-    int lo = 0, hi = n_long - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (__ldcg(&p.items[mid].pad) <= sc.pos) lo = mid; else hi = mid - 1;
-    }
-    const long long base = __ldcg(&p.items[lo].pad);
-    const int nkv = (__ldcg(&p.items[lo].kv1) - __ldcg(&p.items[lo].kv0) + kTileN - 1) / kTileN;
-    const long long off = sc.pos - base;
-    const int h = static_cast<int>(off / nkv), jb = static_cast<int>(off % nkv);
-    const int len = static_cast<int>(min(static_cast<long long>(nkv - jb), sc.end - sc.pos));
-    U = decode_unit(p, lo * p.H + h, n_long);
-    U.jb = jb;
-    U.nt = len;
-    U.split = !(jb == 0 && len == nkv);
-    U.pkind = sc.pos == range_start(sc.W, blockIdx.x, gridDim.x) ? 0 : 1;
-    sc.pos += len;
-    ++sc.k;
-    return true;
-  }
-  if (sc.pk < n_units) {
-    U = decode_unit(p, sc.pk, n_long);
-    sc.pk += gridDim.x;
-    ++sc.k;
-    return true;
-  }
-  return false;
 }
 
 template <int D, int CSB>
@@ -869,10 +782,8 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
       // ---------------------------------------------------------- TMA producer
       uint32_t q_it[2] = {0, 0}, k_it = 0, v_it = 0, cs_it = 0;
       bool ok = true;
-      Sched sc;
-      sched_init(p, sc, n_long);
-      Unit U;
-      while (ok && sched_next(p, sc, n_long, n_units, U)) {
+      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+        const Unit U = decode_unit(p, u, n_long);
         const int ns = U.has_b ? 2 : 1;
         if constexpr (C::CS_BYTES != 0) {
           ok = bounded_wait(bar(B::CS_EMPTY), (cs_it & 1) ^ 1, p, abort_flag,
@@ -898,11 +809,11 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
                         x ? U.q0b : U.q0a);
           ++q_it[x];
         }
-        const int nkv = U.nt;  // K/V tiles of this unit or piece
+        const int nkv = (U.kv1 - U.kv0 + kTileN - 1) / kTileN;
         const int nk = U.shared ? 1 : ns;
         const CUtensorMap* kmap = (U.shared && p.krot) ? &p.tmk_rot : &p.tmk;
         for (int j = 0; j < nkv && ok; ++j) {
-          const int row = U.kv0 + (U.jb + j) * kTileN;
+          const int row = U.kv0 + j * kTileN;
 #pragma unroll
           for (int x = 0; x < 2; ++x) {
             if (x >= nk || !ok) break;
@@ -911,7 +822,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
             ok = bounded_wait(bar(B::K_EMPTY + ks), ((k_it / ST) & 1) ^ 1, p, abort_flag,
                               FRATTN_STATUS_WAIT_TIMEOUT | 0x01);
             if (!ok) break;
-            FR_TRACE(sc.k - 1, 0, j * 2 + x);
+            FR_TRACE((u - (int)blockIdx.x) / (int)gridDim.x, 0, j * 2 + x);
             mbar_arrive_expect_tx(bar(B::K_FULL + ks), C::TILE_BYTES);
 #pragma unroll
             for (int b = 0; b < C::KB; ++b)
@@ -936,15 +847,13 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
       if (lane == 0) {
         uint32_t q_it[2] = {0, 0}, k_it = 0, v_it = 0, p_it[2] = {0, 0};
         bool ok = true;
-        Sched sc;
-        sched_init(p, sc, n_long);
-        Unit U;
-        while (ok && sched_next(p, sc, n_long, n_units, U)) {
-          const int ui = sc.k - 1;
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+          const Unit U = decode_unit(p, u, n_long);
+          const int ui = (u - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x);
           (void)ui;
           const int ns = U.has_b ? 2 : 1;
           const int nk = U.shared ? 1 : ns;
-          const int nkv = U.nt;  // K/V tiles of this unit or piece
+          const int nkv = (U.kv1 - U.kv0 + kTileN - 1) / kTileN;
           int qs[2] = {0, 0};
 #pragma unroll
           for (int x = 0; x < 2; ++x) {
@@ -1039,10 +948,8 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
     bool ok = true;
     const uint8_t* cs_tile = C::CS_BYTES ? smem + C::OFF_CS : nullptr;
     const uint32_t q_lane = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);  // TMEM lane of row r
-    Sched sc;
-    sched_init(p, sc, n_long);
-    Unit U;
-    while (ok && sched_next(p, sc, n_long, n_units, U)) {
+    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+      const Unit U = decode_unit(p, u, n_long);
       const int ns = U.has_b ? 2 : 1;
       if constexpr (C::CS_BYTES != 0) {
         ok = bounded_wait(bar(B::CS_FULL), cs_it & 1, p, abort_flag,
@@ -1082,7 +989,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
         mbar_arrive(bar(B::Q_READY + x * QB + qs));
         ++q_it[x];
       }
-      const int nkv = U.nt;  // K/V tiles of this unit or piece
+      const int nkv = (U.kv1 - U.kv0 + kTileN - 1) / kTileN;
       const int nk = U.shared ? 1 : ns;
       for (int j = 0; j < nkv && ok; ++j) {
 #pragma unroll
@@ -1092,7 +999,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
           ok = bounded_wait(bar(B::K_FULL + ks), (k_it / ST) & 1, p, abort_flag,
                             FRATTN_STATUS_WAIT_TIMEOUT | 0x21);
           if (!ok) break;
-          const int krow = U.kv0 + (U.jb + j) * kTileN;
+          const int krow = U.kv0 + j * kTileN;
           if (!(U.shared && p.krot))  // long segments: K arrives pre-rotated
             rope_tile<D, MODE, TI, TC>(smem + C::OFF_K + ks * C::TILE_BYTES, krow, p, r,
                                        krow == U.q0a ? cs_tile : nullptr);
@@ -1116,17 +1023,15 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
     constexpr int kPolyOf8 = FRATTN_POLY_OF_8;
     uint32_t s_it = 0, o_it = 0;
     bool ok = true;
-    Sched sc;
-    sched_init(p, sc, n_long);
-    Unit U;
-    while (ok && sched_next(p, sc, n_long, n_units, U)) {
-      const int ui = sc.k - 1;
+    for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+      const Unit U = decode_unit(p, u, n_long);
+      const int ui = (u - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x);
       (void)ui;
       if (x == 1 && !U.has_b) continue;
       const int h = x ? U.hb : U.ha;
       const int q0x = x ? U.q0b : U.q0a;
       const int q1x = x ? U.q1b : U.q1a;
-      const int nkv = U.nt;  // K/V tiles of this unit or piece
+      const int nkv = (U.kv1 - U.kv0 + kTileN - 1) / kTileN;
       const int row = q0x + t;
       int lo = 0, hi = 0;
       if (row < q1x) {
@@ -1158,7 +1063,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
         tmem_ld_wait();
         if (t == 0) FR_TRACE(ui, 6, j * 2 + x);
 
-        const int c0 = U.kv0 + (U.jb + j) * kTileN;
+        const int c0 = U.kv0 + j * kTileN;
         const int lo_r = lo - c0, hi_r = hi - c0;
         if (lo_r > 0 || hi_r < kTileN) {
 #pragma unroll
@@ -1251,82 +1156,6 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
 #pragma unroll
       for (int c = 0; c < C::DP / 16; ++c) tmem_ld16(o_addr + c * 16, oo[c]);
       tmem_ld_wait();
-      if (U.split) {
-        // A piece of a unit cut across CTAs: publish this row's partial (O
-        // unnormalised, exponent reference in log2 units, row sum); the warp
-        // that arrives last for these 32 rows merges every piece.
-        constexpr int PS = C::DP + 4;  // floats per partial row (16-byte rows)
-        const int G = static_cast<int>(gridDim.x);
-        auto part = [&](int cta, int kind) -> float* {
-          return p.split_part + (static_cast<size_t>((cta * 2 + kind) * 2 + x) * kTileM + t) * PS;
-        };
-        float* mine = part(blockIdx.x, U.pkind);
-#pragma unroll
-        for (int c = 0; c < C::DP / 16; ++c)
-#pragma unroll
-          for (int e = 0; e < 16; e += 4)
-            *reinterpret_cast<float4*>(mine + c * 16 + e) =
-                make_float4(__uint_as_float(oo[c][e]), __uint_as_float(oo[c][e + 1]),
-                            __uint_as_float(oo[c][e + 2]), __uint_as_float(oo[c][e + 3]));
-        mine[C::DP] = (l > 0.f && m_ref != -INFINITY) ? m_ref * sl2 : -INFINITY;
-        mine[C::DP + 1] = l;
-        __threadfence();
-        __syncwarp();
-        const int item = U.uid / p.H, hh = U.uid % p.H;
-        const long long ustart = static_cast<long long>(__ldcg(&p.items[item].pad)) +
-                                 static_cast<long long>(hh) * ((U.kv1 - U.kv0 + kTileN - 1) / kTileN);
-        const int b0 = range_owner(sc.W, ustart, G);
-        const int b1 = range_owner(sc.W, ustart + (U.kv1 - U.kv0 + kTileN - 1) / kTileN - 1, G);
-        int seen = 0;
-        if (lane == 0) seen = atomicAdd(p.split_cnt + (U.uid * 2 + x) * 4 + (warp & 3), 1);
-        seen = __shfl_sync(0xffffffffu, seen, 0);
-        if (seen == b1 - b0 && store) {
-          __threadfence();
-          float M = -INFINITY;
-          for (int c = b0; c <= b1; ++c) {
-            const int kind = (c > b0 || ustart == range_start(sc.W, c, G)) ? 0 : 1;
-            M = fmaxf(M, __ldcg(part(c, kind) + C::DP));
-          }
-          float acc[C::DP];
-#pragma unroll
-          for (int d = 0; d < C::DP; ++d) acc[d] = 0.f;
-          float L = 0.f;
-          for (int c = b0; c <= b1; ++c) {
-            const int kind = (c > b0 || ustart == range_start(sc.W, c, G)) ? 0 : 1;
-            const float* q = part(c, kind);
-            const float mc = __ldcg(q + C::DP);
-            if (mc == -INFINITY) continue;
-            const float f = ex2(mc - M);
-            L += __ldcg(q + C::DP + 1) * f;
-#pragma unroll
-            for (int d = 0; d < C::DP; d += 4) {
-              const float4 v4 = __ldcg(reinterpret_cast<const float4*>(q + d));
-              acc[d] += v4.x * f;
-              acc[d + 1] += v4.y * f;
-              acc[d + 2] += v4.z * f;
-              acc[d + 3] += v4.w * f;
-            }
-          }
-          const float il = L > 0.f ? 1.f / L : 0.f;
-#pragma unroll
-          for (int c = 0; c < C::DP / 16; ++c) {
-#pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-              if (c * 16 + hf * 8 < D) {
-                uint4 w;
-                const float* a = acc + c * 16 + hf * 8;
-                w.x = pack2<TI>(a[0] * il, a[1] * il);
-                w.y = pack2<TI>(a[2] * il, a[3] * il);
-                w.z = pack2<TI>(a[4] * il, a[5] * il);
-                w.w = pack2<TI>(a[6] * il, a[7] * il);
-                reinterpret_cast<uint4*>(orow + c * 16)[hf] = w;
-              }
-            }
-          }
-        }
-        tc_fence_before();
-        continue;
-      }
 #pragma unroll
       for (int c = 0; c < C::DP / 16; ++c) {
         const uint32_t (&rr)[16] = oo[c];
@@ -1402,7 +1231,7 @@ template <typename TI, int D>
 __global__ void __launch_bounds__(kPrepThreads, 1)
     build_worklist(const int32_t* __restrict__ cu, int nseg, int T, int H, WorkItem* items,
                    int* header, TI* out, int32_t* status, const int32_t* pos_hw,
-                   float* pos_tab, int pos_rows, float theta, int* split_cnt) {
+                   float* pos_tab, int pos_rows, float theta) {
   griddep_launch_dependents();  // dependents only start prologues; they wait for completion
   __shared__ int tmp[64];
   constexpr int kCuSmem = 8192;  // cu_seqlens entries staged in shared memory
@@ -1434,7 +1263,6 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
     if (tid == 0) {
       header[0] = 0;
       header[1] = 0;
-      header[2] = 0;
       if (status)
         atomicCAS(reinterpret_cast<int*>(status), 0,
                   bad ? FRATTN_STATUS_BAD_SEQLENS : FRATTN_STATUS_BAD_POSITIONS);
@@ -1470,20 +1298,17 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
     for (size_t i = tid; i < n1; i += kPrepThreads) o1[i] = z;
   }
 
-  int base = 0, total = 0, wbase = 0, wtotal = 0;
-  // Long items. Each also records (in pad) its first position in the long
-  // work order: units item-major, head-minor, K/V tiles innermost.
+  int base = 0, total = 0;
+  // Long items.
   for (int s0 = 0; s0 < nseg; s0 += kPrepThreads) {
     const int s = s0 + tid;
-    int a = 0, b = 0, n = 0, nkv = 0;
+    int a = 0, b = 0, n = 0;
     if (s < nseg) {
       a = cuv[s];
       b = cuv[s + 1];
       if (b - a > kTileM) n = (b - a + 2 * kTileM - 1) / (2 * kTileM);
-      nkv = (b - a + kTileN - 1) / kTileN;
     }
     const int off = block_exclusive_scan(n, tmp, &total);
-    const int woff = block_exclusive_scan(n * nkv * H, tmp, &wtotal);
     for (int i = 0; i < n; ++i) {
       WorkItem w;
       w.q0 = a + i * 2 * kTileM;
@@ -1493,16 +1318,12 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
       w.seg_lo = s;
       w.seg_hi = s;
       w.kind = kItemLong;
-      w.pad = wbase + woff + i * nkv * H;
+      w.pad = 0;
       items[base + off + i] = w;
     }
     base += total;
-    wbase += wtotal;
   }
   const int n_long = base;
-  // arrival counters of split pieces: [long unit][slot][lane quarter]
-  if (split_cnt != nullptr)
-    for (int i = tid; i < n_long * H * 8; i += kPrepThreads) split_cnt[i] = 0;
   // Packed items: per 128-row chunk, the rows of short segments inside it.
   const int nch = (T + kTileM - 1) / kTileM;
   for (int c0 = 0; c0 < nch; c0 += kPrepThreads) {
@@ -1545,7 +1366,6 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
   if (tid == 0) {
     header[0] = base;
     header[1] = n_long;
-    header[2] = wbase;
   }
 }
 
@@ -1692,24 +1512,8 @@ struct WinCfg {
   static_assert(TMEM_Q + C::DP / 2 <= TMEM_COLS, "TMEM columns");
   // barriers (all single-arrival: TMA transactions or tcgen05 commits)
   static constexpr int Q_FULL = 0, K_FULL = 1, V_FULL = 2, S_FULL = 3, KV_EMPTY = 4, O_FULL = 5,
-                       DONE = 6, COUNT = 7;
+                       COUNT = 6;
 };
-
-// 8 consecutive cos/sin values through ordinary global loads, as fp32.
-template <typename TC>
-__device__ __forceinline__ void load8_plain(const TC* src, float (&v)[8]) {
-  if constexpr (std::is_same<TC, float>::value) {
-    const float4 a = reinterpret_cast<const float4*>(src)[0];
-    const float4 b = reinterpret_cast<const float4*>(src)[1];
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-  } else {
-    const uint4 a = *reinterpret_cast<const uint4*>(src);
-    const TC* h = reinterpret_cast<const TC*>(&a);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = to_f32<TC>(h[i]);
-  }
-}
 
 // Rotate row r of a raw 128 x D tile with cos/sin held in registers (fp32,
 // one rounding to the element type): into TMEM at column qcol as packed pairs
@@ -1754,7 +1558,6 @@ __global__ void __launch_bounds__(kWinThreads, 2) window_attn_kernel(const __gri
   constexpr uint32_t IDESC_O = make_idesc_f16(kBF16, kTileM, C::DP, true);
   constexpr uint32_t SW32 = 6;
   constexpr int MODE = kRopeTable;
-  constexpr int RD = D / 2;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -1764,62 +1567,100 @@ __global__ void __launch_bounds__(kWinThreads, 2) window_attn_kernel(const __gri
   auto bar = [&](int i) -> uint32_t { return bar0 + 8u * static_cast<uint32_t>(i); };
   Ctl* ctl = reinterpret_cast<Ctl*>(smem + W::OFF_BAR + 8 * W::COUNT);
   volatile int* abort_flag = &ctl->abort;
-  // per tile (double-buffered by tile parity): kv0, kv1, first row, end row
-  __shared__ int s_unit[2][4];
-  __shared__ int s_cu[kWinStage];  // all of cu_seqlens when it is short
+  __shared__ int s_unit[6];        // kv0, kv1, first row, end row, staged cu entries, their first index
+  __shared__ int s_cu[kWinStage];  // cu_seqlens, or cu_seqlens[sa .. se + 1] when long
 
   const int t = threadIdx.x;  // q row within the chunk == TMEM lane
   const int warp = t >> 5;
   const int lane = t & 31;
-  const int n_tiles = p.H * ((p.T + kTileM - 1) / kTileM);
-  const int n_all = p.nseg + 1;
-  const bool small = n_all <= kWinStage;
+  const int h = blockIdx.x;
+  const int q0 = blockIdx.y * kTileM;
+  const int q1 = min(q0 + kTileM, p.T);
 #ifdef FRATTN_TRACE
-  // per-CTA global-timer stamps of the first tile: [cta][event], events 0 entry,
-  // 1 unit known, 2 Q rotated, 3 K arrived, 4 S ready, 5 P stored, 6 O ready, 7 tile done
-  const int tr_cta = blockIdx.x;
+  // per-CTA global-timer stamps: [cta][event], events 0 entry, 1 unit known,
+  // 2 Q rotated, 3 K arrived, 4 S ready, 5 P stored, 6 O ready, 7 exit
+  const int tr_cta = blockIdx.y * gridDim.x + blockIdx.x;
 #define WIN_TRACE(ev) \
-  do { if (it == 0 && tr_cta < kTraceWords / 8) g_trace[tr_cta * 8 + (ev)] = globaltimer_ns(); } while (0)
+  do { if (tr_cta < kTraceWords / 8) g_trace[tr_cta * 8 + (ev)] = globaltimer_ns(); } while (0)
 #else
 #define WIN_TRACE(ev) do { } while (0)
 #endif
+  if (t == 0) WIN_TRACE(0);
 
-  // Tile index -> (chunk, head); heads vary fastest so that CTAs running at the
-  // same time share chunks (their cos/sin and cu_seqlens lines).
-  auto tile_q0 = [&](int tile) { return (tile / p.H) * kTileM; };
-  auto tile_h = [&](int tile) { return tile % p.H; };
-  auto load_q = [&](int tile) {  // thread 0
-    mbar_arrive_expect_tx(bar(W::Q_FULL), C::TILE_BYTES);
+  // cos/sin of this thread's q row straight into registers (reused for its K
+  // row when the K tile is the chunk itself, as for windows that do not cross
+  // a chunk boundary); issued first so that the latency overlaps the rest.
+  constexpr int RD = D / 2;
+  float cr[RD], sr[RD];
+  {
+    const int rr = min(q0 + t, p.T - 1);
+    const TC* cp = static_cast<const TC*>(p.cos) + static_cast<size_t>(rr) * RD;
+    const TC* sp = static_cast<const TC*>(p.sin) + static_cast<size_t>(rr) * RD;
+    if constexpr (RD % 8 == 0) {
 #pragma unroll
-    for (int b = 0; b < C::KB; ++b)
-      tma_load_3d(sbase + W::OFF_Q + b * kBlkBytes, &p.tmq, bar(W::Q_FULL), 16 * b, tile_h(tile),
-                  tile_q0(tile));
-  };
-  auto load_k = [&](int tile, int row) {  // thread 0
-    mbar_arrive_expect_tx(bar(W::K_FULL), C::TILE_BYTES);
+      for (int i = 0; i < RD; i += 8) {
+        float a[8], b[8];
+        load8<TC>(cp + i, a);
+        load8<TC>(sp + i, b);
 #pragma unroll
-    for (int b = 0; b < C::KB; ++b)
-      tma_load_3d(sbase + W::OFF_K + b * kBlkBytes, &p.tmk, bar(W::K_FULL), 16 * b, tile_h(tile), row);
-  };
-  auto load_v = [&](int tile, int row) {  // thread 0
-    mbar_arrive_expect_tx(bar(W::V_FULL), C::TILE_BYTES);
+        for (int e = 0; e < 8; ++e) {
+          cr[i + e] = a[e];
+          sr[i + e] = b[e];
+        }
+      }
+    } else {
 #pragma unroll
-    for (int b = 0; b < C::KB; ++b)
-      tma_load_3d(sbase + W::OFF_V + b * kBlkBytes, &p.tmv, bar(W::V_FULL), 16 * b, tile_h(tile), row);
-  };
-  // Segments of a tile's chunk (warp 0): [sa, se] contain rows [a, e) = chunk
-  // rows clipped to [cu[0], cu[nseg]); kv rows [cu[sa], cu[se + 1]). Values are
-  // clamped to [0, T] so that a malformed cu_seqlens (reported below) cannot
-  // send a load or store out of bounds.
-  auto find_unit = [&](int tile, int slot) {
-    const int q0 = tile_q0(tile), q1 = min(q0 + kTileM, p.T);
+      for (int i = 0; i < RD; ++i) {
+        cr[i] = to_f32<TC>(__ldg(cp + i));
+        sr[i] = to_f32<TC>(__ldg(sp + i));
+      }
+    }
+  }
+  const int n_all = p.nseg + 1;
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int i = 0; i < W::COUNT; ++i) mbar_init(bar(i), 1);
+      ctl->abort = 0;
+      fence_mbar_init();
+      fence_proxy_async_smem();
+      // Q does not depend on the segmentation: load first.
+      mbar_arrive_expect_tx(bar(W::Q_FULL), C::TILE_BYTES);
+#pragma unroll
+      for (int b = 0; b < C::KB; ++b)
+        tma_load_3d(sbase + W::OFF_Q + b * kBlkBytes, &p.tmq, bar(W::Q_FULL), 16 * b, h, q0);
+    }
+    __syncwarp();
+    tmem_alloc(smem_u32(&ctl->tmem_base), W::TMEM_COLS);
+    tmem_relinquish();
+  }
+  // cu_seqlens into shared memory in one round of loads when it is short (the
+  // usual case: a few hundred windows); a longer one is searched by warp 0.
+  if (n_all <= kWinStage)
+    for (int i = t; i < n_all; i += kWinThreads) s_cu[i] = __ldg(p.cu + i);
+  if (warp == 1 && blockIdx.x == 0 && blockIdx.y == 0) {
+    // cu_seqlens check (non-decreasing, inside [0, T]) by one warp per call.
+    int bad = 0;
+    for (int sg = lane; sg <= p.nseg; sg += 32) {
+      const int v0 = __ldg(p.cu + sg);
+      if (v0 < 0 || v0 > p.T) bad = 1;
+      if (sg < p.nseg && __ldg(p.cu + sg + 1) < v0) bad = 1;
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0 && p.status)
+      atomicCAS(reinterpret_cast<int*>(p.status), 0, FRATTN_STATUS_BAD_SEQLENS);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // Segments of this chunk: [sa, se] contain rows [a, e) = [q0, q1) clipped
+    // to [cu[0], cu[nseg]); kv rows [cu[sa], cu[se + 1]). Values are clamped
+    // to [0, T] so that a malformed cu_seqlens (reported above) cannot send a
+    // load or store out of bounds.
+    const bool small = n_all <= kWinStage;
     auto cu_at = [&](int i) -> int { return small ? s_cu[i] : __ldg(p.cu + i); };
     const int cu_first = min(max(cu_at(0), 0), p.T);
     const int cu_last = min(max(cu_at(p.nseg), 0), p.T);
     const int a = max(q0, cu_first), e = min(q1, cu_last);
-    int kv0 = 0, kv1 = 0;
+    int kv0 = 0, kv1 = 0, sa = 0, se = -1;
     if (a < e) {
-      int sa, se;
       if (small) {
         sa = upper_bound_smem(s_cu, n_all, a) - 1;
         se = upper_bound_smem(s_cu, n_all, e - 1) - 1;
@@ -1833,338 +1674,253 @@ __global__ void __launch_bounds__(kWinThreads, 2) window_attn_kernel(const __gri
       kv1 = min(max(cu_at(se + 1), 0), p.T);
       if (kv1 < kv0) kv1 = kv0;
     }
+    const int n_stage = se - sa + 2;  // entries cu[sa .. se + 1]
     if (lane == 0) {
-      s_unit[slot][0] = kv0;
-      s_unit[slot][1] = kv1;
-      s_unit[slot][2] = a;
-      s_unit[slot][3] = e;
-    }
-    return make_int2(kv0, kv1);
-  };
-
-  int it = 0;
-  if (t == 0) WIN_TRACE(0);
-  if (warp == 0) {
-    if (lane == 0) {
-      for (int i = 0; i < W::COUNT; ++i) mbar_init(bar(i), 1);
-      ctl->abort = 0;
-      fence_mbar_init();
-      fence_proxy_async_smem();
-      if (static_cast<int>(blockIdx.x) < n_tiles) load_q(blockIdx.x);  // no dependence on cu
+      s_unit[0] = kv0;
+      s_unit[1] = kv1;
+      s_unit[2] = a;
+      s_unit[3] = e;
+      // staged entries for the row lookups: all of cu (base 0) or this chunk's
+      s_unit[4] = a < e ? (small ? n_all : (n_stage <= kWinStage ? n_stage : 0)) : 0;
+      s_unit[5] = small ? 0 : sa;
+      if (kv1 > kv0) {  // first K/V tile right away
+        mbar_arrive_expect_tx(bar(W::K_FULL), C::TILE_BYTES);
+#pragma unroll
+        for (int b = 0; b < C::KB; ++b)
+          tma_load_3d(sbase + W::OFF_K + b * kBlkBytes, &p.tmk, bar(W::K_FULL), 16 * b, h, kv0);
+        mbar_arrive_expect_tx(bar(W::V_FULL), C::TILE_BYTES);
+#pragma unroll
+        for (int b = 0; b < C::KB; ++b)
+          tma_load_3d(sbase + W::OFF_V + b * kBlkBytes, &p.tmv, bar(W::V_FULL), 16 * b, h, kv0);
+      }
     }
     __syncwarp();
-    tmem_alloc(smem_u32(&ctl->tmem_base), W::TMEM_COLS);
-    tmem_relinquish();
-  }
-  // cu_seqlens into shared memory in one round of loads when it is short (the
-  // usual case: a few hundred windows); a longer one is searched in memory.
-  if (small)
-    for (int i = t; i < n_all; i += kWinThreads) s_cu[i] = __ldg(p.cu + i);
-  if (warp == 1 && blockIdx.x == 0) {
-    // cu_seqlens check (non-decreasing, inside [0, T]) by one warp per call.
-    int bad = 0;
-    for (int sg = lane; sg <= p.nseg; sg += 32) {
-      const int v0 = __ldg(p.cu + sg);
-      if (v0 < 0 || v0 > p.T) bad = 1;
-      if (sg < p.nseg && __ldg(p.cu + sg + 1) < v0) bad = 1;
-    }
-    if (__any_sync(0xffffffffu, bad) && lane == 0 && p.status)
-      atomicCAS(reinterpret_cast<int*>(p.status), 0, FRATTN_STATUS_BAD_SEQLENS);
-  }
-  __syncthreads();
-  if (warp == 0 && static_cast<int>(blockIdx.x) < n_tiles) {
-    const int2 kv = find_unit(blockIdx.x, 0);
-    if (lane == 0 && kv.y > kv.x) {
-      load_k(blockIdx.x, kv.x);
-      load_v(blockIdx.x, kv.x);
-    }
+    if (!small && a < e && n_stage <= kWinStage)
+      for (int i = lane; i < n_stage; i += 32) s_cu[i] = __ldg(p.cu + sa + i);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
+  const int kv0 = s_unit[0], kv1 = s_unit[1], ra = s_unit[2], re = s_unit[3], n_cu = s_unit[4];
+  const int cu_base = s_unit[5];
+  const int nkv = (kv1 - kv0 + kTileN - 1) / kTileN;
+  if (t == 0) WIN_TRACE(1);
+
   const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
   const uint32_t s_addr = lane_addr + W::TMEM_S;
   const uint32_t o_addr = lane_addr + W::TMEM_O;
-  const float sl2 = 1.4426950408889634f * rsqrtf(static_cast<float>(D));
-  constexpr float kRescaleLog2 = 8.0f;
-  uint32_t kc = 0;  // K/V tiles consumed (phase of K_FULL, V_FULL, S_FULL, KV_EMPTY)
-  uint32_t oc = 0;  // tiles with K/V work (phase of O_FULL)
+  const int row = q0 + t;
+  int lo = 0, hi = 0;  // kv rows this q row attends to
+  if (row >= ra && row < re) {
+    if (n_cu > 0) {  // staged entries cu[cu_base .. cu_base + n_cu)
+      const int i = min(max(upper_bound_smem(s_cu, n_cu, row), 1), n_cu - 1);
+      lo = max(s_cu[i - 1], kv0);
+      hi = min(s_cu[i], kv1);
+      (void)cu_base;
+    } else {
+      const int sg = upper_bound_cu(p.cu, 0, p.nseg + 1, row) - 1;
+      lo = max(__ldg(p.cu + sg), kv0);
+      hi = min(__ldg(p.cu + sg + 1), kv1);
+    }
+  }
   bool ok = true;
-
-#pragma unroll 1
-  for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
-    const int h = tile_h(tile);
-    const int q0 = tile_q0(tile);
-    const int q1 = min(q0 + kTileM, p.T);
-    const int next = tile + static_cast<int>(gridDim.x);
-    const bool has_next = next < n_tiles;
-    const int kv0 = s_unit[it & 1][0], kv1 = s_unit[it & 1][1];
-    const int ra = s_unit[it & 1][2], re = s_unit[it & 1][3];
-    const int nkv = (kv1 - kv0 + kTileN - 1) / kTileN;
-    if (t == 0) WIN_TRACE(1);
-
-    // cos/sin of this thread's q row into registers (reused for its K row
-    // when the K tile is the chunk itself, as for windows inside the chunk).
-    float cr[RD], sr[RD];
-    {
-      const int rr = min(q0 + t, p.T - 1);
-      const TC* cp = static_cast<const TC*>(p.cos) + static_cast<size_t>(rr) * RD;
-      const TC* sp = static_cast<const TC*>(p.sin) + static_cast<size_t>(rr) * RD;
-      if constexpr (RD % 8 == 0) {
-        // plain (coherent) loads: read-only-path loads could be hoisted by the
-        // compiler above the previous tile's epilogue, doubling register use
-#pragma unroll
-        for (int i = 0; i < RD; i += 8) {
-          float a8[8], b8[8];
-          load8_plain<TC>(cp + i, a8);
-          load8_plain<TC>(sp + i, b8);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            cr[i + e] = a8[e];
-            sr[i + e] = b8[e];
-          }
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < RD; ++i) {
-          cr[i] = to_f32<TC>(cp[i]);
-          sr[i] = to_f32<TC>(sp[i]);
-        }
-      }
-    }
-    const int row = q0 + t;
-    int lo = 0, hi = 0;  // kv rows this q row attends to
-    if (row >= ra && row < re) {
-      if (small) {
-        const int i = min(max(upper_bound_smem(s_cu, n_all, row), 1), n_all - 1);
-        lo = max(s_cu[i - 1], kv0);
-        hi = min(s_cu[i], kv1);
-      } else {
-        const int sg = upper_bound_cu(p.cu, 0, n_all, row) - 1;
-        lo = max(__ldg(p.cu + sg), kv0);
-        hi = min(__ldg(p.cu + sg + 1), kv1);
-      }
-    }
-    float m_ref = -INFINITY, l = 0.f;
-    // Q of this tile (always loaded, so its barrier phase advances every tile)
-    // and K tile 0, both rotated with the register cos/sin (the K tile is the
-    // chunk itself for windows inside the chunk); the registers die here.
-    ok = bounded_wait_warp(bar(W::Q_FULL), it & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x58);
-    if (ok && nkv > 0) {
+  float m_ref = -INFINITY, l = 0.f;
+  if (nkv > 0) {
+    // rotated Q of row t into TMEM (A operand of S)
+    ok = bounded_wait_warp(bar(W::Q_FULL), 0, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x58);
+    if (ok) {
       rope_row_regs<D, TI, true>(smem + W::OFF_Q, t, cr, sr, lane_addr + W::TMEM_Q);
-      if (t == 0) WIN_TRACE(2);
-      ok = bounded_wait_warp(bar(W::K_FULL), kc & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x59);
-      if (ok) {
-        if (t == 0) WIN_TRACE(3);
-        if (kv0 == q0)
-          rope_row_regs<D, TI, false>(smem + W::OFF_K, t, cr, sr, 0);
-        else
-          rope_tile<D, MODE, TI, TC>(smem + W::OFF_K, kv0, p, t, nullptr);
-        fence_proxy_async_smem();
-      }
       tmem_st_wait();
     }
-    tc_fence_before();
-    ok = __syncthreads_and(ok);
-    tc_fence_after();
-    if (!ok) break;
-    auto issue_s = [&]() {  // thread 0: S = Q K^T (Q from TMEM)
-      const uint64_t kdesc = make_sdesc(sbase + W::OFF_K, 16, 256, SW32);
-#pragma unroll
-      for (int kb = 0; kb < C::KB; ++kb)
-        umma_ts(tmem + W::TMEM_S, tmem + W::TMEM_Q + kb * 8,
-                kdesc + static_cast<uint64_t>((kb * kBlkBytes) >> 4), IDESC_S, kb > 0 ? 1u : 0u);
-      umma_commit(bar(W::S_FULL));
-    };
-    // The Q buffer is free: the next tile's Q, and (warp 0) its segments,
-    // while the first S runs.
-    int2 next_kv = make_int2(0, 0);
-    if (t == 0) {
-      if (nkv > 0) issue_s();
-      if (has_next) load_q(next);
+    if (t == 0) WIN_TRACE(2);
+    // K tile 0: rotated before the tile loop, with the register cos/sin when the
+    // tile is this chunk (they are dead afterwards).
+    ok = ok && bounded_wait_warp(bar(W::K_FULL), 0, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x59);
+    if (ok) {
+      if (t == 0) WIN_TRACE(3);
+      if (kv0 == q0)
+        rope_row_regs<D, TI, false>(smem + W::OFF_K, t, cr, sr, 0);
+      else
+        rope_tile<D, MODE, TI, TC>(smem + W::OFF_K, kv0, p, t, nullptr);
+      fence_proxy_async_smem();
     }
-    if (warp == 0 && has_next) next_kv = find_unit(next, (it + 1) & 1);
-    if (nkv > 0) {
-#pragma unroll 1
-      for (int j = 0; j < nkv; ++j, ++kc) {
-        const int krow = kv0 + j * kTileN;
-        if (j > 0) {  // further K/V tiles of this chunk (segments crossing chunk edges)
-          if (t == 0) {
-            ok = bounded_wait(bar(W::KV_EMPTY), (kc - 1) & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x51);
-            if (ok) {
-              load_k(tile, krow);
-              load_v(tile, krow);
-            }
-          }
-          ok = ok && bounded_wait_warp(bar(W::K_FULL), kc & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x59);
-          if (ok) {
-            rope_tile<D, MODE, TI, TC>(smem + W::OFF_K, krow, p, t, nullptr);
-            fence_proxy_async_smem();
-          }
-          tc_fence_before();
-          ok = __syncthreads_and(ok);
-          tc_fence_after();
-          if (!ok) break;
-          if (t == 0) issue_s();
-        }
-        ok = bounded_wait_warp(bar(W::S_FULL), kc & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x5A);
-        ok = __syncthreads_and(ok);  // every warp leaves the loop together
-        if (!ok) break;
-        if (t == 0 && j == 0) WIN_TRACE(4);
-        tc_fence_after();
-        // The K buffer is free after the last S of the tile: the next tile's first K.
-        if (t == 0 && j == nkv - 1 && has_next && next_kv.y > next_kv.x) load_k(next, next_kv.x);
-        const int lo_r = lo - krow, hi_r = hi - krow;
-        // 32-column chunks that no row of this warp attends to keep P = 0 and
-        // cost no exponentials (the other windows of the tile).
-        uint32_t live = 0;
+    const float sl2 = 1.4426950408889634f * rsqrtf(static_cast<float>(D));
+    constexpr float kRescaleLog2 = 8.0f;
+    for (int j = 0; j < nkv; ++j) {
+      const int krow = kv0 + j * kTileN;
+      if (j > 0 && t == 0) {  // next K/V tile once PV(j-1) has released the buffers
+        ok = bounded_wait(bar(W::KV_EMPTY), (j - 1) & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x51);
+        if (ok) {
+          mbar_arrive_expect_tx(bar(W::K_FULL), C::TILE_BYTES);
 #pragma unroll
-        for (int c = 0; c < kTileN / 32; ++c)
-          if (__any_sync(0xffffffffu, lo_r < 32 * c + 32 && hi_r > 32 * c)) live |= 1u << c;
-        float s[kTileN];
+          for (int b = 0; b < C::KB; ++b)
+            tma_load_3d(sbase + W::OFF_K + b * kBlkBytes, &p.tmk, bar(W::K_FULL), 16 * b, h, krow);
+          mbar_arrive_expect_tx(bar(W::V_FULL), C::TILE_BYTES);
 #pragma unroll
-        for (int c = 0; c < kTileN / 32; ++c) {
-          uint32_t rr[32];
-          if (live & (1u << c)) {
-            tmem_ld32(s_addr + c * 32, rr);
-#pragma unroll
-            for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(rr[e]);
-          }
-        }
-        tmem_ld_wait();
-        float mxq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int c = 0; c < kTileN / 32; ++c) {
-          if (!(live & (1u << c))) continue;
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int i = c * 32 + e;
-            if (i < lo_r || i >= hi_r) s[i] = -INFINITY;
-          }
-#pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-              mxq[q] = max3(mxq[q], s[c * 32 + e + 2 * q], s[c * 32 + e + 2 * q + 1]);
-          }
-        }
-        const float mx = max3(fmaxf(mxq[0], mxq[1]), mxq[2], mxq[3]);
-        float alpha = 1.f;
-        bool rescale = false;
-        if (mx > m_ref && (m_ref == -INFINITY || (mx - m_ref) * sl2 > kRescaleLog2)) {
-          alpha = (m_ref == -INFINITY) ? 0.f : ex2((m_ref - mx) * sl2);
-          rescale = l > 0.f;
-          m_ref = mx;
-        }
-        const float mb = (m_ref == -INFINITY ? 0.f : m_ref) * sl2;
-        const uint64_t scale2 = f2pack(sl2, sl2);
-        const uint64_t bias2 = f2pack(-mb, -mb);
-        uint64_t sp2[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int c = 0; c < kTileN / 32; ++c) {
-          uint32_t pk[16];
-          if (live & (1u << c)) {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const uint64_t xa = fma2(f2pack(s[c * 32 + 2 * e], s[c * 32 + 2 * e + 1]), scale2, bias2);
-              float a0, a1;
-              f2unpack(xa, a0, a1);
-              const uint64_t pp = f2pack(ex2(a0), ex2(a1));
-              sp2[e & 3] = add2(sp2[e & 3], pp);
-              float p0, p1;
-              f2unpack(pp, p0, p1);
-              pk[e] = pack2<TI>(p0, p1);
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) pk[e] = 0u;
-          }
-          tmem_st16(s_addr + c * 16, pk);
-        }
-        float sa_, sb_, sc_, sd_;
-        f2unpack(add2(sp2[0], sp2[1]), sa_, sb_);
-        f2unpack(add2(sp2[2], sp2[3]), sc_, sd_);
-        l = l * alpha + ((sa_ + sb_) + (sc_ + sd_));
-        // O holds PV(j-1) complete: S(j) was issued after it by the same thread.
-        if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll
-          for (int c = 0; c < C::DP / 16; ++c) {
-            uint32_t rr[16];
-            tmem_ld16(o_addr + c * 16, rr);
-            tmem_ld_wait();
-#pragma unroll
-            for (int e = 0; e < 16; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
-            tmem_st16(o_addr + c * 16, rr);
-          }
-        }
-        if (t == 0 && j == 0) WIN_TRACE(5);
-        tmem_st_wait();
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
-        if (t == 0) {  // O += P V (P from TMEM, where it overwrote S)
-          ok = bounded_wait(bar(W::V_FULL), kc & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x54);
-          if (ok) {
-            const uint64_t vdesc = make_sdesc(sbase + W::OFF_V, kBlkBytes, 256, SW32);
-#pragma unroll
-            for (int kk = 0; kk < kTileN / 16; ++kk)
-              umma_ts(tmem + W::TMEM_O, tmem + W::TMEM_S + kk * 8,
-                      vdesc + static_cast<uint64_t>((kk * 512) >> 4), IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
-            umma_commit(bar(W::KV_EMPTY));
-            if (j == nkv - 1) umma_commit(bar(W::O_FULL));
-          }
+          for (int b = 0; b < C::KB; ++b)
+            tma_load_3d(sbase + W::OFF_V + b * kBlkBytes, &p.tmv, bar(W::V_FULL), 16 * b, h, krow);
         }
       }
+      // rotated K row t (in place, shared memory); tile 0 was rotated above
+      if (j > 0) {
+        ok = ok && bounded_wait_warp(bar(W::K_FULL), j & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x59);
+        if (ok) {
+          rope_tile<D, MODE, TI, TC>(smem + W::OFF_K, krow, p, t, nullptr);
+          fence_proxy_async_smem();
+        }
+      }
+      tc_fence_before();
       ok = __syncthreads_and(ok);
-      if (ok) ok = bounded_wait_warp(bar(W::O_FULL), oc & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x5B);
-      ++oc;
-      if (t == 0) WIN_TRACE(6);
       tc_fence_after();
-      // The V buffer is free after the last PV: the next tile's first V.
-      if (ok && t == 0 && has_next && next_kv.y > next_kv.x) load_v(next, next_kv.x);
-    } else if (t == 0 && has_next && next_kv.y > next_kv.x) {
-      load_k(next, next_kv.x);  // nothing of this tile used the K/V buffers
-      load_v(next, next_kv.x);
-    }
-    // Epilogue: normalise and store the row; rows outside every segment are 0.
-    // (The TMEM loads are warp-wide; only the stores depend on the row.)
-    {
-      TI* orow = static_cast<TI*>(p.out) + (static_cast<size_t>(min(row, p.T - 1)) * p.H + h) * D;
-      const bool has = ok && lo < hi && l > 0.f;
-      const float inv_l = has ? 1.f / l : 0.f;
+      if (!ok) break;
+      if (t == 0) {  // S = Q K^T (Q from TMEM)
+        const uint64_t kdesc = make_sdesc(sbase + W::OFF_K, 16, 256, SW32);
 #pragma unroll
-      for (int c = 0; c < C::DP / 16; ++c) {
-        uint32_t rr[16];
-        if (nkv > 0) {
+        for (int kb = 0; kb < C::KB; ++kb)
+          umma_ts(tmem + W::TMEM_S, tmem + W::TMEM_Q + kb * 8,
+                  kdesc + static_cast<uint64_t>((kb * kBlkBytes) >> 4), IDESC_S, kb > 0 ? 1u : 0u);
+        umma_commit(bar(W::S_FULL));
+      }
+      ok = bounded_wait_warp(bar(W::S_FULL), j & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x5A);
+      if (!ok) break;
+      if (t == 0 && j == 0) WIN_TRACE(4);
+      tc_fence_after();
+      const int lo_r = lo - krow, hi_r = hi - krow;
+      // 32-column chunks that no row of this warp attends to keep P = 0 and
+      // cost no exponentials (the other windows of the tile).
+      uint32_t live = 0;
+#pragma unroll
+      for (int c = 0; c < kTileN / 32; ++c)
+        if (__any_sync(0xffffffffu, lo_r < 32 * c + 32 && hi_r > 32 * c)) live |= 1u << c;
+      float s[kTileN];
+#pragma unroll
+      for (int c = 0; c < kTileN / 32; ++c) {
+        uint32_t rr[32];
+        if (live & (1u << c)) {
+          tmem_ld32(s_addr + c * 32, rr);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(rr[e]);
+        }
+      }
+      tmem_ld_wait();
+      float mxq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < kTileN / 32; ++c) {
+        if (!(live & (1u << c))) continue;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int i = c * 32 + e;
+          if (i < lo_r || i >= hi_r) s[i] = -INFINITY;
+        }
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            mxq[q] = max3(mxq[q], s[c * 32 + e + 2 * q], s[c * 32 + e + 2 * q + 1]);
+        }
+      }
+      const float mx = max3(fmaxf(mxq[0], mxq[1]), mxq[2], mxq[3]);
+      float alpha = 1.f;
+      bool rescale = false;
+      if (mx > m_ref && (m_ref == -INFINITY || (mx - m_ref) * sl2 > kRescaleLog2)) {
+        alpha = (m_ref == -INFINITY) ? 0.f : ex2((m_ref - mx) * sl2);
+        rescale = l > 0.f;
+        m_ref = mx;
+      }
+      const float mb = (m_ref == -INFINITY ? 0.f : m_ref) * sl2;
+      const uint64_t scale2 = f2pack(sl2, sl2);
+      const uint64_t bias2 = f2pack(-mb, -mb);
+      uint64_t sp2[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int c = 0; c < kTileN / 32; ++c) {
+        uint32_t pk[16];
+        if (live & (1u << c)) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const uint64_t xa = fma2(f2pack(s[c * 32 + 2 * e], s[c * 32 + 2 * e + 1]), scale2, bias2);
+            float a0, a1;
+            f2unpack(xa, a0, a1);
+            const uint64_t pp = f2pack(ex2(a0), ex2(a1));
+            sp2[e & 3] = add2(sp2[e & 3], pp);
+            float p0, p1;
+            f2unpack(pp, p0, p1);
+            pk[e] = pack2<TI>(p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) pk[e] = 0u;
+        }
+        tmem_st16(s_addr + c * 16, pk);
+      }
+      float sa_, sb_, sc_, sd_;
+      f2unpack(add2(sp2[0], sp2[1]), sa_, sb_);
+      f2unpack(add2(sp2[2], sp2[3]), sc_, sd_);
+      l = l * alpha + ((sa_ + sb_) + (sc_ + sd_));
+      // O holds PV(j-1) complete: S(j) was issued after it by the same thread.
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+        for (int c = 0; c < C::DP / 16; ++c) {
+          uint32_t rr[16];
           tmem_ld16(o_addr + c * 16, rr);
           tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
+          tmem_st16(o_addr + c * 16, rr);
         }
-        uint4 w0, w1;
-        w0.x = pack2<TI>(has ? __uint_as_float(rr[0]) * inv_l : 0.f, has ? __uint_as_float(rr[1]) * inv_l : 0.f);
-        w0.y = pack2<TI>(has ? __uint_as_float(rr[2]) * inv_l : 0.f, has ? __uint_as_float(rr[3]) * inv_l : 0.f);
-        w0.z = pack2<TI>(has ? __uint_as_float(rr[4]) * inv_l : 0.f, has ? __uint_as_float(rr[5]) * inv_l : 0.f);
-        w0.w = pack2<TI>(has ? __uint_as_float(rr[6]) * inv_l : 0.f, has ? __uint_as_float(rr[7]) * inv_l : 0.f);
-        w1.x = pack2<TI>(has ? __uint_as_float(rr[8]) * inv_l : 0.f, has ? __uint_as_float(rr[9]) * inv_l : 0.f);
-        w1.y = pack2<TI>(has ? __uint_as_float(rr[10]) * inv_l : 0.f, has ? __uint_as_float(rr[11]) * inv_l : 0.f);
-        w1.z = pack2<TI>(has ? __uint_as_float(rr[12]) * inv_l : 0.f, has ? __uint_as_float(rr[13]) * inv_l : 0.f);
-        w1.w = pack2<TI>(has ? __uint_as_float(rr[14]) * inv_l : 0.f, has ? __uint_as_float(rr[15]) * inv_l : 0.f);
-        if (row < q1) {
-          if (c * 16 < D) reinterpret_cast<uint4*>(orow + c * 16)[0] = w0;
-          if (c * 16 + 8 < D) reinterpret_cast<uint4*>(orow + c * 16)[1] = w1;
+      }
+      if (t == 0 && j == 0) WIN_TRACE(5);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncthreads();
+      tc_fence_after();
+      if (t == 0) {  // O += P V (P from TMEM, where it overwrote S)
+        ok = bounded_wait(bar(W::V_FULL), j & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x54);
+        if (ok) {
+          const uint64_t vdesc = make_sdesc(sbase + W::OFF_V, kBlkBytes, 256, SW32);
+#pragma unroll
+          for (int kk = 0; kk < kTileN / 16; ++kk)
+            umma_ts(tmem + W::TMEM_O, tmem + W::TMEM_S + kk * 8,
+                    vdesc + static_cast<uint64_t>((kk * 512) >> 4), IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(bar(W::KV_EMPTY));
+          if (j == nkv - 1) umma_commit(bar(W::O_FULL));
         }
       }
     }
-    if (t == 0) WIN_TRACE(7);
-    // the next tile reads s_unit[(it + 1) & 1] and may overwrite O / S / Q columns
-    tc_fence_before();
-    __syncthreads();
+    ok = __syncthreads_and(ok);
+    if (ok) ok = bounded_wait_warp(bar(W::O_FULL), 0, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x5B);
+    if (t == 0) WIN_TRACE(6);
     tc_fence_after();
   }
-  // Drain before TMEM is released: every MMA issued by thread 0 has completed.
-  if (t == 0) {
-    umma_commit(bar(W::DONE));
-    bounded_wait(bar(W::DONE), 0, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x5C);
+  // Epilogue: normalise and store the row; rows outside every segment are 0.
+  // (The TMEM loads are warp-wide; only the stores depend on the row.)
+  {
+    TI* orow = static_cast<TI*>(p.out) + (static_cast<size_t>(min(row, p.T - 1)) * p.H + h) * D;
+    const bool has = ok && lo < hi && l > 0.f;
+    const float inv_l = has ? 1.f / l : 0.f;
+    uint32_t oo[C::DP / 16][16];
+    if (nkv > 0) {
+#pragma unroll
+      for (int c = 0; c < C::DP / 16; ++c) tmem_ld16(o_addr + c * 16, oo[c]);
+      tmem_ld_wait();
+    }
+#pragma unroll
+    for (int c = 0; c < C::DP / 16; ++c) {
+      const uint32_t (&rr)[16] = oo[c];
+      uint4 w0, w1;
+      w0.x = pack2<TI>(has ? __uint_as_float(rr[0]) * inv_l : 0.f, has ? __uint_as_float(rr[1]) * inv_l : 0.f);
+      w0.y = pack2<TI>(has ? __uint_as_float(rr[2]) * inv_l : 0.f, has ? __uint_as_float(rr[3]) * inv_l : 0.f);
+      w0.z = pack2<TI>(has ? __uint_as_float(rr[4]) * inv_l : 0.f, has ? __uint_as_float(rr[5]) * inv_l : 0.f);
+      w0.w = pack2<TI>(has ? __uint_as_float(rr[6]) * inv_l : 0.f, has ? __uint_as_float(rr[7]) * inv_l : 0.f);
+      w1.x = pack2<TI>(has ? __uint_as_float(rr[8]) * inv_l : 0.f, has ? __uint_as_float(rr[9]) * inv_l : 0.f);
+      w1.y = pack2<TI>(has ? __uint_as_float(rr[10]) * inv_l : 0.f, has ? __uint_as_float(rr[11]) * inv_l : 0.f);
+      w1.z = pack2<TI>(has ? __uint_as_float(rr[12]) * inv_l : 0.f, has ? __uint_as_float(rr[13]) * inv_l : 0.f);
+      w1.w = pack2<TI>(has ? __uint_as_float(rr[14]) * inv_l : 0.f, has ? __uint_as_float(rr[15]) * inv_l : 0.f);
+      if (row < q1) {
+        if (c * 16 < D) reinterpret_cast<uint4*>(orow + c * 16)[0] = w0;
+        if (c * 16 + 8 < D) reinterpret_cast<uint4*>(orow + c * 16)[1] = w1;
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -2172,6 +1928,7 @@ __global__ void __launch_bounds__(kWinThreads, 2) window_attn_kernel(const __gri
     tc_fence_after();
     tmem_dealloc(tmem, W::TMEM_COLS);
   }
+  if (t == 0) WIN_TRACE(7);
 #undef WIN_TRACE
 }
 
@@ -2197,9 +1954,7 @@ int launch_window(const Params& prm, cudaStream_t st) {
         return FRATTN_E_CUDA;
       attr_set |= bit;
     }
-    // persistent: two CTAs per SM walk the (chunk, head) tiles
-    const long long tiles = static_cast<long long>(prm.H) * ((prm.T + kTileM - 1) / kTileM);
-    const int grid = static_cast<int>(std::min<long long>(tiles, 2LL * sm_count_for_current_device()));
+    const dim3 grid(prm.H, (prm.T + kTileM - 1) / kTileM);
     kern<<<grid, kWinThreads, W::SMEM_BYTES, st>>>(prm);
     return cudaGetLastError() == cudaSuccess ? 0 : FRATTN_E_CUDA;
   }
