@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--no-encoder", action="store_true", help="skip the 32-layer encoder timing")
     ap.add_argument("--no-dp", action="store_true", help="skip the config-5 data-parallel sweep")
     ap.add_argument("--no-comparators", action="store_true", help="skip the same-box GPU comparators")
+    ap.add_argument("--profile", choices=["windowed", "full"], default=None,
+                    help="profiling case for ncu: run --warmup + --steps eager calls of one layer kind and exit")
+    ap.add_argument("--images", type=int, default=1, help="896x896 images per call in --profile mode")
     return ap.parse_args()
 
 
@@ -465,21 +468,35 @@ def run_ours(args):
             for var in variants:
                 call(s[var], var)
     torch.cuda.synchronize()
-    # Every graph also records an event pair around its attention kernel(s)
-    # (frattn_set_timing_events), read after the timed replays: the kernel's
-    # own duration beside the per-call time.
+    graphs = []
+    for s in sets:
+        gs = {}
+        for var in variants:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                call(s[var], var)
+            gs[var] = g
+        graphs.append(gs)
+    # Probe graphs: the same calls with an event pair recorded around the
+    # attention kernel(s) (frattn_set_timing_events), replayed right after the
+    # timed loop: the kernel's own duration beside the per-call time. (Event
+    # nodes inside the timed graphs would add their own latency to the step.)
     from fused_rope_attn_b200 import _lib as flib
-    graphs, kev = [], []
+    probes, kev = [], []
     for s in sets:
         gs, ke = {}, {}
         for var in variants:
             g = torch.cuda.CUDAGraph()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            # a first record creates the CUDA events (torch creates them lazily)
+            # and lets torch read their timestamps once the graph re-records them
+            e0.record(stream)
+            e1.record(stream)
             with torch.cuda.graph(g, stream=stream):
                 flib.load().frattn_set_timing_events(e0.cuda_event, e1.cuda_event)
                 call(s[var], var)
             gs[var], ke[var] = g, (e0, e1)
-        graphs.append(gs)
+        probes.append(gs)
         kev.append(ke)
     torch.cuda.synchronize()
 
@@ -510,9 +527,16 @@ def run_ours(args):
     clk = clocks.stop()
     elapsed_ms = e_start.elapsed_time(e_end)
     per_var = {var: statistics.mean(a.elapsed_time(b) for a, b in ev[var]) for var in variants}
-    # last replay of each graph inside the timed loop (R samples per layer kind)
-    kern_var = {var: statistics.mean(kev[i][var][0].elapsed_time(kev[i][var][1]) for i in range(min(R, K)))
-                for var in variants}
+    kern = {var: [] for var in variants}
+    for rep_ in range(2):
+        for i in range(R):
+            for var in variants:
+                with torch.cuda.stream(stream):
+                    probes[i][var].replay()
+                torch.cuda.synchronize()
+                if rep_:
+                    kern[var].append(kev[i][var][0].elapsed_time(kev[i][var][1]))
+    kern_var = {var: statistics.mean(kern[var]) for var in variants}
     status = last_status(dev)
     # The timed outputs come from graph replays: check them against eager calls.
     graph_err = 0.0
@@ -634,8 +658,29 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_profile_case(args):
+    """A few eager calls of one layer kind on ``--images`` 896x896 images (for
+    ncu: the kernel of interest launches once per call, after the warm-up)."""
+    import torch
+    from fused_rope_attn_b200 import fused_rope_attention, last_status
+    global GRID
+    GRID = [(1, 64, 64)] * args.images
+    dev = torch.device("cuda", 0)
+    sets, T = make_inputs(torch, dev, seed=0)
+    t = sets[args.profile]
+    hint = 64 if args.profile == "windowed" else 4096
+    for _ in range(args.warmup + args.steps):
+        fused_rope_attention(t["q"], t["k"], t["v"], t["cos"], t["sin"], t["cu"], max_seqlen=hint)
+    torch.cuda.synchronize()
+    assert last_status(dev) == 0
+    print(json.dumps({"profile": args.profile, "images": args.images, "tokens": T, "calls": args.warmup + args.steps}))
+
+
 def main():
     args = parse()
+    if args.profile:
+        run_profile_case(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
