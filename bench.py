@@ -55,8 +55,9 @@ def parse():
     ap.add_argument("--no-encoder", action="store_true", help="skip the 32-layer encoder timing")
     ap.add_argument("--no-dp", action="store_true", help="skip the config-5 data-parallel sweep")
     ap.add_argument("--no-comparators", action="store_true", help="skip the same-box GPU comparators")
-    ap.add_argument("--profile", choices=["windowed", "full"], default=None,
-                    help="profiling case for ncu: run --warmup + --steps eager calls of one layer kind and exit")
+    ap.add_argument("--profile", choices=["windowed", "full", "encoder"], default=None,
+                    help="profiling case: windowed/full run --warmup + --steps eager calls of one layer kind "
+                         "(for ncu); encoder prints a per-kernel breakdown of one 1344x1344 forward per arm")
     ap.add_argument("--images", type=int, default=1, help="896x896 images per call in --profile mode")
     return ap.parse_args()
 
@@ -658,6 +659,38 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def encoder_breakdown():
+    """Per-kernel CUDA time of one 1344x1344 32-layer encoder forward, fused and
+    unfused attention (torch profiler, after two warm-up forwards)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    from fused_rope_attn_b200.encoder import EncoderConfig, VisionEncoder, encoder_inputs
+    grid = [(1, 96, 96)]
+    cfg = EncoderConfig()
+    enc = VisionEncoder(cfg, device="cuda", dtype=torch.bfloat16)
+    x = encoder_inputs(grid, cfg.hidden, seed=0, device="cuda")
+    plan = enc.plan(grid)
+    for attn in ("fused", "unfused"):
+        for _ in range(2):
+            enc(x, grid, attn=attn, plan=plan)
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            enc(x, grid, attn=attn, plan=plan)
+            torch.cuda.synchronize()
+        rows = []
+        for e in prof.key_averages():
+            t = getattr(e, "self_device_time_total", None)
+            if t is None:
+                t = e.self_cuda_time_total
+            if t > 0:
+                rows.append((t, e.count, e.key))
+        rows.sort(reverse=True)
+        total = sum(r[0] for r in rows)
+        print(f"== {attn}: {total / 1e3:.2f} ms of kernel time")
+        for t, c, k in rows[:14]:
+            print(f"{t / 1e3:9.3f} ms {100 * t / total:5.1f} % {c:5d}x  {k[:90]}")
+
+
 def run_profile_case(args):
     """A few eager calls of one layer kind on ``--images`` 896x896 images (for
     ncu: the kernel of interest launches once per call, after the warm-up)."""
@@ -678,6 +711,9 @@ def run_profile_case(args):
 
 def main():
     args = parse()
+    if args.profile == "encoder":
+        encoder_breakdown()
+        return
     if args.profile:
         run_profile_case(args)
         return
