@@ -86,3 +86,34 @@ def test_noalloc_rejects_oversize_before_touching_the_gpu():
                                 _lib.BF16, 16, None, None)
     assert rc == _lib.E_NOALLOC_LIMIT
     assert "NOALLOC" in _lib.error_string(rc)
+
+
+def test_strided_entry_point_validates_strides():
+    lib = _lib.load()
+
+    def fwd(qs, ks, vs, **kw):
+        a = dict(T=128, H=2, D=80)
+        a.update(kw)
+        return lib.frattn_fwd_strided(16, 16, 16, qs, ks, vs, 16, 16, _lib.F32, 16, 1, a["T"], a["H"], a["D"], 0,
+                                      _lib.BF16, 16, 16, 1 << 20, None, None)
+    assert fwd(0, 160, 160) == _lib.E_SHAPE          # strides must be given
+    assert fwd(150, 160, 160) == _lib.E_SHAPE        # below H * D
+    assert fwd(164, 160, 160) == _lib.E_ALIGN        # row starts not 16-byte aligned
+    assert lib.frattn_set_timing_events(16, None) == _lib.E_NULL
+    assert lib.frattn_set_timing_events(None, None) == 0
+
+
+def test_window_plan_sizes_match_host():
+    import ctypes
+    from fused_rope_attn_b200.utils import get_window_index
+    lib = _lib.load()
+    for grid in ([(1, 32, 32)], [(1, 22, 30), (2, 8, 12)], [(8, 32, 32), (1, 64, 64)]):
+        arr = (ctypes.c_int32 * (3 * len(grid)))(*[v for g in grid for v in g])
+        u, w, ws = ctypes.c_int64(0), ctypes.c_int64(0), ctypes.c_size_t(0)
+        assert lib.frattn_window_plan_sizes(arr, len(grid), 112, 2, 14, ctypes.byref(u), ctypes.byref(w),
+                                            ctypes.byref(ws)) == 0
+        widx, cu = get_window_index(grid)
+        assert u.value == widx.numel() and w.value == cu.numel() - 1 and ws.value >= 32 * len(grid)
+    bad = (ctypes.c_int32 * 3)(1, 15, 16)  # h not divisible by the merge size
+    assert lib.frattn_window_plan_sizes(bad, 1, 112, 2, 14, ctypes.byref(u), ctypes.byref(w),
+                                        ctypes.byref(ws)) == _lib.E_SHAPE
