@@ -22,10 +22,10 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, q, fail_rank):
+def _worker(rank, world, port, q, fail_rank, timeout_s):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import datetime
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
     try:
         if rank == fail_rank:
             raise RuntimeError("injected rank failure")
@@ -44,11 +44,13 @@ def _worker(rank, world, port, q, fail_rank):
             pass
 
 
-def _run(world, fail_rank=-1):
+def _run(world, fail_rank=-1, timeout_s=120):
+    # (a generous process-group timeout: a spawned rank can take many seconds to
+    # import torch on a loaded machine; the failure test shortens it)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=_worker, args=(r, world, port, q, fail_rank)) for r in range(world)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, q, fail_rank, timeout_s)) for r in range(world)]
     for p in ps:
         p.start()
     msgs = [q.get(timeout=120) for _ in range(world)]
@@ -93,6 +95,6 @@ def test_dp_two_ranks_matches_single_process():
 
 
 def test_dp_rank_failure_is_reported_not_hung():
-    msgs = _run(2, fail_rank=1)
+    msgs = _run(2, fail_rank=1, timeout_s=20)
     kinds = sorted(m[0] for m in msgs)
     assert kinds == ["error", "error"], msgs
