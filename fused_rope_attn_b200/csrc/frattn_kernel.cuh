@@ -553,34 +553,34 @@ __global__ void __launch_bounds__(256) rotate_k_long(const __grid_constant__ Par
         kout[base + j] = from_f32<TI>(x0 * c - x1 * sn);
         kout[base + D / 2 + j] = from_f32<TI>(x0 * sn + x1 * c);
       }
-      continue;
-    }
-    uint4 ua[NP], ub[NP];
+    } else {
+      uint4 ua[NP], ub[NP];
 #pragma unroll
-    for (int c = 0; c < NP; ++c) {
-      ua[c] = __ldg(reinterpret_cast<const uint4*>(kin + ibase + 8 * c));
-      ub[c] = __ldg(reinterpret_cast<const uint4*>(kin + ibase + D / 2 + 8 * c));
-    }
-#pragma unroll
-    for (int c = 0; c < NP; ++c) {
-      float x0[8], x1[8], cs[8], sn[8];
-      unpack8<TI>(ua[c], x0);
-      unpack8<TI>(ub[c], x1);
-      rope_coeffs<D, MODE, TC>(p, row, 8 * c, cs, sn);
-      uint4 oa, ob;
-      uint32_t* wa = reinterpret_cast<uint32_t*>(&oa);
-      uint32_t* wb = reinterpret_cast<uint32_t*>(&ob);
-#pragma unroll
-      for (int q = 0; q < 8; q += 2) {
-        const float a0 = x0[q] * cs[q] - x1[q] * sn[q];
-        const float a1 = x0[q + 1] * cs[q + 1] - x1[q + 1] * sn[q + 1];
-        const float b0 = x0[q] * sn[q] + x1[q] * cs[q];
-        const float b1 = x0[q + 1] * sn[q + 1] + x1[q + 1] * cs[q + 1];
-        wa[q / 2] = pack2<TI>(a0, a1);
-        wb[q / 2] = pack2<TI>(b0, b1);
+      for (int c = 0; c < NP; ++c) {
+        ua[c] = __ldg(reinterpret_cast<const uint4*>(kin + ibase + 8 * c));
+        ub[c] = __ldg(reinterpret_cast<const uint4*>(kin + ibase + D / 2 + 8 * c));
       }
-      *reinterpret_cast<uint4*>(kout + base + 8 * c) = oa;
-      *reinterpret_cast<uint4*>(kout + base + D / 2 + 8 * c) = ob;
+#pragma unroll
+      for (int c = 0; c < NP; ++c) {
+        float x0[8], x1[8], cs[8], sn[8];
+        unpack8<TI>(ua[c], x0);
+        unpack8<TI>(ub[c], x1);
+        rope_coeffs<D, MODE, TC>(p, row, 8 * c, cs, sn);
+        uint4 oa, ob;
+        uint32_t* wa = reinterpret_cast<uint32_t*>(&oa);
+        uint32_t* wb = reinterpret_cast<uint32_t*>(&ob);
+#pragma unroll
+        for (int q = 0; q < 8; q += 2) {
+          const float a0 = x0[q] * cs[q] - x1[q] * sn[q];
+          const float a1 = x0[q + 1] * cs[q + 1] - x1[q + 1] * sn[q + 1];
+          const float b0 = x0[q] * sn[q] + x1[q] * cs[q];
+          const float b1 = x0[q + 1] * sn[q + 1] + x1[q + 1] * cs[q + 1];
+          wa[q / 2] = pack2<TI>(a0, a1);
+          wb[q / 2] = pack2<TI>(b0, b1);
+        }
+        *reinterpret_cast<uint4*>(kout + base + 8 * c) = oa;
+        *reinterpret_cast<uint4*>(kout + base + D / 2 + 8 * c) = ob;
+      }
     }
   }
 }
