@@ -281,7 +281,7 @@ def encoder_timing(torch, dev, reps=10):
     plan = enc.plan(grid)
     res, outs = {}, {}
     s = torch.cuda.Stream(device=dev)
-    for attn in ("fused", "unfused"):
+    for attn in ("fused", "fused_qkv", "unfused"):
         with torch.cuda.stream(s):
             for _ in range(2):
                 enc(x, grid, attn=attn, plan=plan)
@@ -304,9 +304,70 @@ def encoder_timing(torch, dev, reps=10):
     fl = encoder_flops(grid, cfg)
     return {"image": "1344x1344 (9216 tokens, 144 windows + 1 full segment)", "layers": cfg.depth,
             "fused_ms": res["fused"], "unfused_ms": res["unfused"], "speedup": res["unfused"] / res["fused"],
+            "fused_qkv_ms": res["fused_qkv"], "speedup_fused_qkv": res["unfused"] / res["fused_qkv"],
+            "fused_qkv_arm": "QKV projection with RoPE in its epilogue (frattn_qkv_rope) + attention on "
+                             "pre-rotated q/k (frattn_fwd_rotated)",
+            "fused_qkv_vs_fused_rel_l2": rel_l2(outs["fused_qkv"], outs["fused"]),
             "unfused_arm": "RoPE in bf16 (torch elementwise) + " + unfused_backend(),
             "gemm_tflop": fl["gemm"] / 1e12, "attention_tflop": fl["attention"] / 1e12,
             "fused_vs_unfused_rel_l2": rel_l2(outs["fused"], outs["unfused"]), "launch": "CUDA graph replay"}
+
+
+def projection_timing(torch, dev, peak_tflops, reps=50):
+    """One encoder layer's QKV projection at 1344x1344 (9216 x 1280 -> 3840): the
+    tcgen05 GEMM with RoPE in its epilogue against cuBLAS (torch linear) alone and
+    cuBLAS + the reference caller's separate RoPE (bench.py:72-78). CUDA-graph
+    replay of each arm, 8 rotating inputs (> L2 together), CUDA events."""
+    from fused_rope_attn_b200 import qkv_rope_projection
+    from fused_rope_attn_b200.encoder import rope_unfused
+    T, K, H, D = 9216, 1280, 16, 80
+    g = torch.Generator(device=dev).manual_seed(0)
+    xs = [torch.randn(T, K, generator=g, device=dev).to(torch.bfloat16) for _ in range(8)]
+    w = (torch.randn(3 * H * D, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(3 * H * D, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    ang = torch.rand(T, D // 2, generator=g, device=dev) * 50
+    cos, sin = ang.cos(), ang.sin()
+    outs = [torch.empty(T, 3, H, D, dtype=torch.bfloat16, device=dev) for _ in range(8)]
+
+    def ours(i):
+        qkv_rope_projection(xs[i], w, b, cos, sin, H, out=outs[i])
+
+    def cublas(i):
+        torch.nn.functional.linear(xs[i], w, b)
+
+    def cublas_rope(i):
+        qkv = torch.nn.functional.linear(xs[i], w, b).view(T, 3, H, D)
+        return rope_unfused(qkv[:, 0], cos, sin), rope_unfused(qkv[:, 1], cos, sin)
+
+    res = {}
+    s = torch.cuda.Stream(device=dev)
+    for name, fn in (("ours_us", ours), ("cublas_linear_us", cublas), ("cublas_plus_rope_us", cublas_rope)):
+        with torch.cuda.stream(s):
+            for i in range(8):
+                fn(i)
+        torch.cuda.synchronize(dev)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=s):
+            for i in range(8):
+                fn(i)
+        gr.replay()
+        torch.cuda.synchronize(dev)
+        a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            gr.replay()
+        e.record()
+        torch.cuda.synchronize(dev)
+        res[name] = a.elapsed_time(e) * 1e3 / (reps * 8)
+        del gr
+    flop = 2.0 * T * K * 3 * H * D
+    tf = flop / (res["ours_us"] * 1e-6) / 1e12
+    res.update({"shape": f"[{T}, {K}] x [{K}, {3 * H * D}] + bias, RoPE on q/k", "tflop": flop / 1e12,
+                "ours_tflops": tf, "ours_frac_of_bf16_peak": tf / peak_tflops,
+                "cublas_tflops": flop / (res["cublas_linear_us"] * 1e-6) / 1e12,
+                "speedup_vs_cublas_plus_rope": res["cublas_plus_rope_us"] / res["ours_us"],
+                "kernel": "qkv_rope_gemm_kernel (tcgen05, TMA 128-B swizzle, persistent, TMEM double buffer)"})
+    return res
 
 
 # --------------------------------------------------------------------------- config 5
@@ -646,6 +707,10 @@ def run_ours(args):
             except Exception as exc:  # noqa: BLE001
                 line["gpu_comparators"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
         if not args.no_encoder:
+            try:
+                line["qkv_projection"] = projection_timing(torch, dev, tflops)
+            except Exception as exc:  # noqa: BLE001
+                line["qkv_projection"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
             try:
                 line["encoder"] = encoder_timing(torch, dev)
             except Exception as exc:  # noqa: BLE001 - report, do not lose the main line

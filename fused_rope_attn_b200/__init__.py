@@ -7,10 +7,12 @@ Drop-in for the reference module ``fused_attn`` of sdan/fused-rope-attn
 from .fused_attn import (  # noqa: F401
     SUPPORTED_HEAD_DIMS,
     compute_rope_2d,
+    fused_attention_rotated,
     fused_rope_attention,
     fused_rope_attention_pos,
     last_status,
     next_pow2,
+    qkv_rope_projection,
     rope_positions_2d,
 )
 

@@ -12,7 +12,7 @@ namespace frattn {
 
 #define FRATTN_DECL(DD)                                                                       \
   int attn_d##DD(const Params& prm, int mode, int in_dtype, int cs_dtype, cudaStream_t st);   \
-  int window_d##DD(const Params& prm, int in_dtype, int cs_dtype, cudaStream_t st);            \
+  int window_d##DD(const Params& prm, int in_dtype, int cs_dtype, bool rotated, cudaStream_t st); \
   int prep_d##DD(const int32_t* cu, int nseg, int T, int H, WorkItem* items, int* header,     \
                  void* out, int32_t* status, const int32_t* pos_hw, float* pos_tab,           \
                  int pos_rows, float theta, int in_dtype, cudaStream_t st);
@@ -136,10 +136,11 @@ int dispatch_head_dim(const Params& prm, int mode, int D, int in_dtype, int cs_d
 }
 
 // Window kernel of head dimension D (FRATTN_E_SHAPE: none for this D / type).
-int dispatch_window(const Params& prm, int D, int in_dtype, int cs_dtype, cudaStream_t st) {
+int dispatch_window(const Params& prm, int D, int in_dtype, int cs_dtype, bool rotated,
+                    cudaStream_t st) {
   switch (D) {
 #define FRATTN_CASE(DD) \
-    case DD: return window_d##DD(prm, in_dtype, cs_dtype, st);
+    case DD: return window_d##DD(prm, in_dtype, cs_dtype, rotated, st);
 #ifdef FRATTN_FAST_BUILD
     FRATTN_CASE(80)
 #else
@@ -217,6 +218,8 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
     if (cs_dtype != FRATTN_F32 && cs_dtype != FRATTN_F16 && cs_dtype != FRATTN_BF16)
       return FRATTN_E_DTYPE;
     if (!aligned16(cos) || !aligned16(sin)) return FRATTN_E_ALIGN;
+  } else if (MODE == kRopeNone) {
+    frattn_workspace_bytes(T, nseg, &need);
   } else {
     if (!pos_hw) return FRATTN_E_NULL;
     if (max_position <= 0 || max_position > 65536) return FRATTN_E_SHAPE;
@@ -254,7 +257,7 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
   const size_t krot_off = (need + 255) & ~size_t(255);
   const size_t krot_bytes = static_cast<size_t>(T) * H * D * 2;
   const bool no_long = max_seqlen > 0 && max_seqlen <= kTileM;
-  if (ws_bytes >= krot_off + krot_bytes && !no_long) {
+  if (MODE != kRopeNone && ws_bytes >= krot_off + krot_bytes && !no_long) {
     prm.krot = ws + krot_off;
     if (make_qkv_map(&prm.tmk_rot, prm.krot, T, H, D, bf16, static_cast<long long>(H) * D))
       return FRATTN_E_TMAP;
@@ -284,9 +287,9 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
   // Window regime (the caller says no segment exceeds one tile): one kernel,
   // no work list. Head dims / element types without a window kernel, and the
   // position entry point, take the general path below.
-  if (MODE == kRopeTable && no_long) {
+  if (MODE != kRopePos && no_long) {
     timing_begin(st);  // the window kernel is then the only launch of the call
-    rc = dispatch_window(prm, D, in_dtype, cs_dtype, st);
+    rc = dispatch_window(prm, D, in_dtype, cs_dtype, MODE == kRopeNone, st);
     if (rc != FRATTN_E_SHAPE) {
       timing_end(st);
       return rc;
@@ -302,6 +305,11 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
 }
 
 }  // namespace
+
+namespace frattn {
+// Bounded-wait limit shared by every kernel of the library (frattn_set_wait_limit_ns).
+unsigned long long frattn_wait_limit_ns() { return g_wait_limit_ns; }
+}  // namespace frattn
 
 // ---------------------------------------------------------------- no-alloc variant
 // Work-list storage for frattn_fwd_noalloc: a fixed device array that every GPU
@@ -406,6 +414,16 @@ int frattn_fwd_pos(const void* q, const void* k, const void* v, const int32_t* p
   return fwd_impl<kRopePos>(q, k, v, nullptr, nullptr, FRATTN_F32, pos_hw, max_position, theta,
                             cu_seqlens, nseg, T, H, D, in_dtype, out, workspace, workspace_bytes,
                             status, stream, max_seqlen);
+}
+
+int frattn_fwd_rotated(const void* q, const void* k, const void* v, long long q_stride,
+                       long long k_stride, long long v_stride, const int32_t* cu_seqlens, int nseg,
+                       int T, int H, int D, int max_seqlen, int in_dtype, void* out,
+                       void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  if (q_stride < 0 || k_stride < 0 || v_stride < 0) return FRATTN_E_SHAPE;
+  return fwd_impl<kRopeNone>(q, k, v, nullptr, nullptr, FRATTN_F32, nullptr, 0, 0.f, cu_seqlens,
+                             nseg, T, H, D, in_dtype, out, workspace, workspace_bytes, status,
+                             stream, max_seqlen, q_stride, k_stride, v_stride);
 }
 
 int frattn_selftest_wait_timeout(int32_t* status, uint64_t limit_ns, void* stream) {

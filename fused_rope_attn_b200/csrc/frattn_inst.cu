@@ -19,16 +19,19 @@ int FRATTN_CAT(attn_d, FRATTN_D)(const Params& prm, int mode, int in_dtype, int 
   return dispatch_in<FRATTN_D, kRopeTable>(prm, in_dtype, cs_dtype, st);
 #else
   if (mode == kRopePos) return dispatch_in<FRATTN_D, kRopePos>(prm, in_dtype, cs_dtype, st);
+  if (mode == kRopeNone) return dispatch_in<FRATTN_D, kRopeNone>(prm, in_dtype, cs_dtype, st);
   return dispatch_in<FRATTN_D, kRopeTable>(prm, in_dtype, cs_dtype, st);
 #endif
 }
 
 // Window-regime kernel (every segment at most 128 tokens); FRATTN_E_SHAPE when
 // this head dim or element type has none.
-int FRATTN_CAT(window_d, FRATTN_D)(const Params& prm, int in_dtype, int cs_dtype, cudaStream_t st) {
-  if (in_dtype == FRATTN_BF16) return window_cs<FRATTN_D, __nv_bfloat16>(prm, cs_dtype, st);
+// `rotated`: q and k arrive rotated (no tables are read).
+int FRATTN_CAT(window_d, FRATTN_D)(const Params& prm, int in_dtype, int cs_dtype, bool rotated,
+                                   cudaStream_t st) {
+  if (in_dtype == FRATTN_BF16) return window_cs<FRATTN_D, __nv_bfloat16>(prm, cs_dtype, st, rotated);
 #ifndef FRATTN_FAST_BUILD
-  if (in_dtype == FRATTN_F16) return window_cs<FRATTN_D, __half>(prm, cs_dtype, st);
+  if (in_dtype == FRATTN_F16) return window_cs<FRATTN_D, __half>(prm, cs_dtype, st, rotated);
 #endif
   return FRATTN_E_DTYPE;
 }

@@ -102,8 +102,9 @@ __host__ __device__ inline size_t max_items(int T) {
   return 3 * chunks + 2;
 }
 
-// Rotary angle source: materialised tables (reference API) or (h, w) ids.
-enum RopeMode : int { kRopeTable = 0, kRopePos = 1 };
+// Rotary angle source: materialised tables (reference API), (h, w) ids, or
+// none (q and k arrive rotated, e.g. from the QKV projection's epilogue).
+enum RopeMode : int { kRopeTable = 0, kRopePos = 1, kRopeNone = 2 };
 
 struct Params {
   CUtensorMap tmq, tmk, tmv;
@@ -459,7 +460,9 @@ __device__ __forceinline__ void rope_row_elementwise(uint8_t* tile, int row0, co
 template <int D, int MODE, typename TI, typename TC>
 __device__ __forceinline__ void rope_tile(uint8_t* tile, int row0, const Params& p, int r0,
                                           const uint8_t* cs_smem = nullptr) {
-  if constexpr (D % 16 == 0) {
+  if constexpr (MODE == kRopeNone) {
+    return;  // already rotated
+  } else if constexpr (D % 16 == 0) {
     // One chunk pair per iteration, as a real loop: the rotation shares the
     // SM's instruction caches with the softmax code, and the unrolled form
     // (D/16 copies at each call site) measured slower in the window regime.
@@ -484,6 +487,11 @@ __device__ __forceinline__ void rope_q_to_tmem(const uint8_t* tile, int row0, co
   for (int c = 0; c < NP; ++c) {
     const uint4 ua = *reinterpret_cast<const uint4*>(tile + chunk_off(r, c));
     const uint4 ub = *reinterpret_cast<const uint4*>(tile + chunk_off(r, c + NP));
+    if constexpr (MODE == kRopeNone) {  // already rotated: copy
+      tmem_st4(qcol + 4 * c, ua);
+      tmem_st4(qcol + 4 * (c + NP), ub);
+      continue;
+    }
     float cs[8], sn[8];
     if (MODE == kRopeTable && cs_smem != nullptr) {
       const TC* cst = reinterpret_cast<const TC*>(cs_smem) + r * (D / 2) + c * 8;
@@ -1406,11 +1414,12 @@ int launch_attn(const Params& prm, cudaStream_t st) {
   lc.stream = st;
   lc.attrs = &attr;
   lc.numAttrs = 1;
-  if (prm.krot) {
+  if (MODE != kRopeNone && prm.krot) {
     lc.gridDim = dim3(2 * grid);
     lc.blockDim = dim3(256);
     lc.dynamicSmemBytes = 0;
-    if (cudaLaunchKernelEx(&lc, rotate_k_long<D, MODE, TI, TC>, prm) != cudaSuccess) return FRATTN_E_CUDA;
+    if constexpr (MODE != kRopeNone)
+      if (cudaLaunchKernelEx(&lc, rotate_k_long<D, MODE, TI, TC>, prm) != cudaSuccess) return FRATTN_E_CUDA;
   }
   lc.gridDim = dim3(grid);
   lc.blockDim = dim3(kThreads);
@@ -1421,7 +1430,7 @@ int launch_attn(const Params& prm, cudaStream_t st) {
 
 template <int D, int MODE, typename TI>
 int dispatch_cs(const Params& prm, int cs_dtype, cudaStream_t st) {
-  if constexpr (MODE == kRopePos) return launch_attn<D, MODE, TI, float>(prm, st);
+  if constexpr (MODE != kRopeTable) return launch_attn<D, MODE, TI, float>(prm, st);
 #ifdef FRATTN_FAST_BUILD  // experiment builds: fp32 tables only
   if (cs_dtype != FRATTN_F32) return FRATTN_E_DTYPE;
   return launch_attn<D, MODE, TI, float>(prm, st);
@@ -1518,7 +1527,7 @@ struct WinCfg {
 // Rotate row r of a raw 128 x D tile with cos/sin held in registers (fp32,
 // one rounding to the element type): into TMEM at column qcol as packed pairs
 // (TO_TMEM) or in place in shared memory.
-template <int D, typename TI, bool TO_TMEM>
+template <int D, typename TI, bool TO_TMEM, bool ROT = true>
 __device__ __forceinline__ void rope_row_regs(uint8_t* tile, int r, const float (&cr)[D / 2],
                                               const float (&sr)[D / 2], uint32_t qcol) {
   static_assert(D % 16 == 0, "whole 8-element chunks");
@@ -1527,6 +1536,13 @@ __device__ __forceinline__ void rope_row_regs(uint8_t* tile, int r, const float 
   for (int c = 0; c < NP; ++c) {
     const uint4 ua = *reinterpret_cast<const uint4*>(tile + chunk_off(r, c));
     const uint4 ub = *reinterpret_cast<const uint4*>(tile + chunk_off(r, c + NP));
+    if constexpr (!ROT) {  // already rotated: copy to TMEM (in place: nothing to do)
+      if constexpr (TO_TMEM) {
+        tmem_st4(qcol + 4 * c, ua);
+        tmem_st4(qcol + 4 * (c + NP), ub);
+      }
+      continue;
+    }
     float x0[8], x1[8];
     unpack8<TI>(ua, x0);
     unpack8<TI>(ub, x1);
@@ -1549,15 +1565,16 @@ __device__ __forceinline__ void rope_row_regs(uint8_t* tile, int r, const float 
   }
 }
 
-template <int D, typename TI, typename TC>
+template <int D, typename TI, typename TC, int MODE = kRopeTable>
 __global__ void __launch_bounds__(kWinThreads, 2) window_attn_kernel(const __grid_constant__ Params p) {
+  static_assert(MODE == kRopeTable || MODE == kRopeNone, "window kernel: tables or pre-rotated");
+  constexpr bool kRot = MODE == kRopeTable;
   using C = Cfg<D, static_cast<int>(sizeof(TC))>;
   using W = WinCfg<D, static_cast<int>(sizeof(TC))>;
   constexpr bool kBF16 = std::is_same<TI, __nv_bfloat16>::value;
   constexpr uint32_t IDESC_S = make_idesc_f16(kBF16, kTileM, kTileN, false);
   constexpr uint32_t IDESC_O = make_idesc_f16(kBF16, kTileM, C::DP, true);
   constexpr uint32_t SW32 = 6;
-  constexpr int MODE = kRopeTable;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -1592,7 +1609,7 @@ __global__ void __launch_bounds__(kWinThreads, 2) window_attn_kernel(const __gri
   // a chunk boundary); issued first so that the latency overlaps the rest.
   constexpr int RD = D / 2;
   float cr[RD], sr[RD];
-  {
+  if constexpr (kRot) {
     const int rr = min(q0 + t, p.T - 1);
     const TC* cp = static_cast<const TC*>(p.cos) + static_cast<size_t>(rr) * RD;
     const TC* sp = static_cast<const TC*>(p.sin) + static_cast<size_t>(rr) * RD;
@@ -1730,7 +1747,7 @@ __global__ void __launch_bounds__(kWinThreads, 2) window_attn_kernel(const __gri
     // rotated Q of row t into TMEM (A operand of S)
     ok = bounded_wait_warp(bar(W::Q_FULL), 0, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x58);
     if (ok) {
-      rope_row_regs<D, TI, true>(smem + W::OFF_Q, t, cr, sr, lane_addr + W::TMEM_Q);
+      rope_row_regs<D, TI, true, kRot>(smem + W::OFF_Q, t, cr, sr, lane_addr + W::TMEM_Q);
       tmem_st_wait();
     }
     if (t == 0) WIN_TRACE(2);
@@ -1740,7 +1757,7 @@ __global__ void __launch_bounds__(kWinThreads, 2) window_attn_kernel(const __gri
     if (ok) {
       if (t == 0) WIN_TRACE(3);
       if (kv0 == q0)
-        rope_row_regs<D, TI, false>(smem + W::OFF_K, t, cr, sr, 0);
+        rope_row_regs<D, TI, false, kRot>(smem + W::OFF_K, t, cr, sr, 0);
       else
         rope_tile<D, MODE, TI, TC>(smem + W::OFF_K, kv0, p, t, nullptr);
       fence_proxy_async_smem();
@@ -1934,13 +1951,13 @@ __global__ void __launch_bounds__(kWinThreads, 2) window_attn_kernel(const __gri
 
 // Launch of the window kernel; FRATTN_E_SHAPE when this head dim has none
 // (the caller then uses the general path).
-template <int D, typename TI, typename TC>
+template <int D, typename TI, typename TC, int MODE = kRopeTable>
 int launch_window(const Params& prm, cudaStream_t st) {
   if constexpr (!(Cfg<D, static_cast<int>(sizeof(TC))>::Q_TMEM)) {
     return FRATTN_E_SHAPE;
   } else {
     using W = WinCfg<D, static_cast<int>(sizeof(TC))>;
-    auto kern = window_attn_kernel<D, TI, TC>;
+    auto kern = window_attn_kernel<D, TI, TC, MODE>;
     static unsigned long long attr_set = 0;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1961,7 +1978,8 @@ int launch_window(const Params& prm, cudaStream_t st) {
 }
 
 template <int D, typename TI>
-int window_cs(const Params& prm, int cs_dtype, cudaStream_t st) {
+int window_cs(const Params& prm, int cs_dtype, cudaStream_t st, bool rotated = false) {
+  if (rotated) return launch_window<D, TI, float, kRopeNone>(prm, st);
 #ifdef FRATTN_FAST_BUILD
   if (cs_dtype != FRATTN_F32) return FRATTN_E_SHAPE;
   return launch_window<D, TI, float>(prm, st);

@@ -15,6 +15,9 @@ window permutation.
 
 Attention implementations (``attn=``):
 * ``"fused"``    — ``fused_rope_attention`` (this repository's sm_100a kernel);
+* ``"fused_qkv"`` — the QKV projection with RoPE in its epilogue
+                   (``qkv_rope_projection``, an own tcgen05 GEMM) followed by
+                   ``fused_attention_rotated``: no rotation in attention;
 * ``"unfused"``  — separate RoPE in the input dtype (torch elementwise, as the
                    reference's baseline ``bench.py:73-78``) + FlashAttention
                    varlen (``flash_attn_varlen_func``; ``torch.nn.attention.varlen``
@@ -27,7 +30,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-from .fused_attn import compute_rope_2d, fused_rope_attention
+from .fused_attn import compute_rope_2d, fused_attention_rotated, fused_rope_attention, qkv_rope_projection
 from .utils import get_window_index, segments_per_image, window_shuffle, window_unshuffle
 
 __all__ = ["EncoderConfig", "VisionEncoder", "encoder_inputs", "rope_unfused", "attention_fp32"]
@@ -173,7 +176,8 @@ class VisionEncoder(torch.nn.Module):
                 attn_hook=None):
         """Run the stack. ``layer_hook(i, h)`` sees the hidden states after layer i;
         ``attn_hook(i, q, k, v, cos, sin, cu_seqlens, o)`` sees each attention call's
-        inputs and output (window order)."""
+        inputs and output (window order; with ``"fused_qkv"`` q and k are already
+        rotated)."""
         c = self.cfg
         plan = plan or self.plan(grid_thw)
         T = x.shape[0]
@@ -183,9 +187,14 @@ class VisionEncoder(torch.nn.Module):
             cu = plan["cu_full"] if full else plan["cu_win"]
             max_len = plan["max_full"] if full else plan["max_win"]
             y = self._rms(h, L["n1"])
-            qkv = torch.nn.functional.linear(y, L["qkv_w"], L["qkv_b"]).view(T, 3, c.heads, c.head_dim)
+            if attn == "fused_qkv":  # q, k leave the projection rotated
+                qkv = qkv_rope_projection(y, L["qkv_w"], L["qkv_b"], plan["cos"], plan["sin"], c.heads)
+            else:
+                qkv = torch.nn.functional.linear(y, L["qkv_w"], L["qkv_b"]).view(T, 3, c.heads, c.head_dim)
             q, k, v = qkv[:, 0], qkv[:, 1], qkv[:, 2]
-            if attn == "fused":
+            if attn == "fused_qkv":
+                o = fused_attention_rotated(q, k, v, cu, max_seqlen=max_len)
+            elif attn == "fused":
                 o = fused_rope_attention(q, k, v, plan["cos"], plan["sin"], cu, max_seqlen=max_len)
             elif attn == "unfused":
                 o = _attn_unfused(q, k, v, plan["cos"], plan["sin"], cu, max_len)

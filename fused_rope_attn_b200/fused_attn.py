@@ -395,3 +395,113 @@ def fused_rope_attention_pos(
         )
     _lib.check(rc, "frattn_fwd_pos")
     return out
+
+
+# --------------------------------------------------------------------------- rotation in the projection
+QKV_ROPE_HEAD_DIMS = (32, 48, 64, 80, 96, 112, 128)
+
+
+def qkv_rope_projection(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    bias: torch.Tensor | None,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    num_heads: int,
+    *,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """QKV projection with the 2D rotary embedding applied in the GEMM epilogue.
+
+    ``x`` ``[T, K]`` (rows may be strided), ``weight`` ``[3 * num_heads * head_dim, K]``
+    (``nn.Linear`` layout: q rows, then k, then v), ``bias`` ``[3 * H * D]`` or None,
+    ``cos``/``sin`` ``[T, head_dim // 2]`` as for ``fused_rope_attention``.
+    Returns ``[T, 3, H, D]`` with the q and k heads rotated and v as projected:
+    ``linear(x, weight, bias)`` rounded to x's dtype, then rotated in fp32 and
+    rounded again (the reference's caller rotates q/k in a separate pass after
+    the projection, bench.py:72-78). Feed ``[:, 0]``, ``[:, 1]``, ``[:, 2]`` to
+    ``fused_attention_rotated``.
+    """
+    if x.device.type != "cuda":
+        raise ValueError(f"x must be on CUDA, got device={x.device}")
+    if x.ndim != 2 or weight.ndim != 2 or weight.shape[1] != x.shape[1]:
+        raise ValueError(f"x must be [T, K] and weight [N, K], got x={tuple(x.shape)} weight={tuple(weight.shape)}")
+    if x.dtype not in (torch.float16, torch.bfloat16) or weight.dtype != x.dtype:
+        raise ValueError(f"x and weight must share dtype float16 or bfloat16, got {x.dtype} / {weight.dtype}")
+    T, K = (int(s) for s in x.shape)
+    N = int(weight.shape[0])
+    if num_heads <= 0 or N % (3 * num_heads):
+        raise ValueError(f"weight rows {N} are not 3 * num_heads * head_dim for num_heads={num_heads}")
+    hd = N // (3 * num_heads)
+    if hd not in QKV_ROPE_HEAD_DIMS:
+        raise ValueError(f"head_dim {hd} is not supported by the QKV projection kernel ({QKV_ROPE_HEAD_DIMS})")
+    if K % 8:
+        raise ValueError(f"K={K} must be a multiple of 8 (16-byte rows)")
+    if cos.shape != (T, hd // 2) or sin.shape != (T, hd // 2):
+        raise ValueError(f"cos/sin must be [T, head_dim//2]={T, hd // 2}, got cos={tuple(cos.shape)} sin={tuple(sin.shape)}")
+    if cos.dtype not in _DT or sin.dtype not in _DT:
+        raise ValueError(f"cos/sin dtype must be float16, bfloat16 or float32, got {cos.dtype} / {sin.dtype}")
+    if sin.dtype != cos.dtype:
+        sin = sin.to(cos.dtype)
+    if bias is not None and (bias.shape != (N,) or bias.dtype != x.dtype):
+        raise ValueError(f"bias must be [{N}] of dtype {x.dtype}, got {tuple(bias.shape)} {bias.dtype}")
+    if not (x.stride(1) == 1 and x.stride(0) >= K and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0):
+        x = _aligned(x.contiguous())
+    xs = int(x.stride(0))
+    w = _aligned(weight.contiguous())
+    b = _aligned(bias.contiguous()) if bias is not None else None
+    cos = _aligned(cos.to(x.device).contiguous())
+    sin = _aligned(sin.to(x.device).contiguous())
+    if out is None:
+        out = torch.empty(T, 3, num_heads, hd, dtype=x.dtype, device=x.device)
+    elif out.shape != (T, 3, num_heads, hd) or out.dtype != x.dtype or not out.is_contiguous() or out.data_ptr() % 16:
+        raise ValueError(f"out must be a contiguous 16-byte aligned [{T}, 3, {num_heads}, {hd}] {x.dtype} tensor")
+    if T == 0:
+        return out
+    lib = _lib.load()
+    with torch.cuda.device(x.device):
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        rc = lib.frattn_qkv_rope(
+            x.data_ptr(), xs, w.data_ptr(), b.data_ptr() if b is not None else None, cos.data_ptr(),
+            sin.data_ptr(), _DT[cos.dtype], T, K, num_heads, hd, _DT[x.dtype], out.data_ptr(),
+            _status_word(x.device).data_ptr(), stream,
+        )
+    _lib.check(rc, "frattn_qkv_rope")
+    return out
+
+
+def fused_attention_rotated(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    cu_seqlens: torch.Tensor,
+    *,
+    out: torch.Tensor | None = None,
+    max_seqlen: int | None = None,
+) -> torch.Tensor:
+    """Varlen attention for q and k that are already rotated (``qkv_rope_projection``).
+
+    ``fused_rope_attention`` without the tables: same shapes, dtypes, ``cu_seqlens``
+    and ``max_seqlen`` contract, same kernels minus the rotation.
+    """
+    total, heads, hd = _check_qkv(q, k, v)
+    if hd not in KERNEL_HEAD_DIMS:
+        raise ValueError(f"head_dim {hd} is not supported (multiples of 8 in [32, 128])")
+    if cu_seqlens.ndim != 1 or cu_seqlens.numel() < 2:
+        raise ValueError(f"cu_seqlens must be 1D with length >= 2, got {tuple(cu_seqlens.shape)}")
+    (q, qs), (k, ks), (v, vs) = (_token_rows(t) for t in (q, k, v))
+    out = _check_out(out, q)
+    cu = _check_cu(cu_seqlens, q.device)
+    nseg = cu.numel() - 1
+    lib = _lib.load()
+    ws_bytes = _lib.workspace_bytes(total, nseg)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    with torch.cuda.device(q.device):
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+        rc = lib.frattn_fwd_rotated(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), qs, ks, vs, cu.data_ptr(), nseg, total, heads, hd,
+            int(max_seqlen or 0), _DT[q.dtype], out.data_ptr(), ws.data_ptr(), ws_bytes,
+            _status_word(q.device).data_ptr(), stream,
+        )
+    _lib.check(rc, "frattn_fwd_rotated")
+    return out

@@ -137,6 +137,33 @@ int frattn_fwd_pos(const void* q, const void* k, const void* v, const int32_t* p
                    int H, int D, int max_seqlen, int in_dtype, void* out, void* workspace,
                    size_t workspace_bytes, int32_t* status, void* stream);
 
+/* ---- Rotation in the QKV projection (the reference's caller rotates q/k in
+ * a separate elementwise pass after the projection, bench.py:72-78, or the
+ * fused kernel rotates them per q block, fused_attn.py:340-345, 385-390).
+ *
+ * frattn_qkv_rope: qkv = x W^T + bias on the tensor cores (tcgen05, fp32
+ * accumulation in TMEM) with the rotary embedding applied in the epilogue:
+ *   x    : [T, K] rows of x_stride elements (0: K), element type in_dtype
+ *   w    : [3 H D, K] contiguous (nn.Linear weight layout, q rows, then k, then v)
+ *   bias : [3 H D] or NULL
+ *   cos, sin : [T, D/2] (cs_dtype F32 / F16 / BF16), rows of token t
+ *   qkv  : [T, 3, H, D] contiguous output; q and k heads rotated, v as projected
+ * Each output value is acc + bias rounded to in_dtype; q/k values are then
+ * rotated in fp32 and rounded once more (what frattn_fwd does to a stored q/k).
+ * D a multiple of 16 in [32, 128]; K and x_stride multiples of 8.
+ *
+ * frattn_fwd_rotated: frattn_fwd_strided for q and k that are already rotated
+ * (e.g. the q/k views of frattn_qkv_rope's output, strides 3 H D; 0 means
+ * contiguous): no tables are read and no rotation runs. Workspace as frattn_fwd.
+ */
+int frattn_qkv_rope(const void* x, long long x_stride, const void* w, const void* bias,
+                    const void* cos, const void* sin, int cs_dtype, int T, int K, int H, int D,
+                    int in_dtype, void* qkv, int32_t* status, void* stream);
+int frattn_fwd_rotated(const void* q, const void* k, const void* v, long long q_stride,
+                       long long k_stride, long long v_stride, const int32_t* cu_seqlens, int nseg,
+                       int T, int H, int D, int max_seqlen, int in_dtype, void* out,
+                       void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
 /* Allocation-free variant of frattn_fwd (no counterpart in the reference).
  *
  * For callers that cannot allocate device memory at the point of the call: a

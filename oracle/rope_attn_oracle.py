@@ -22,6 +22,9 @@ Functions and the reference lines they restate:
 * ``varlen_attention``                — utils.py:178-193 (non-causal softmax(QK^T d^-1/2)V
                                         per cu_seqlens segment; scale fused_attn.py:354-355)
 * ``rope_attention``                  — the unfused path: apply_rope then varlen_attention
+* ``qkv_rope``                        — the caller's projection + separate rotation
+                                        (bench.py:72-78: linear output in the input
+                                        type, then the split-half rotation of q, k)
 """
 from __future__ import annotations
 
@@ -38,6 +41,7 @@ __all__ = [
     "apply_rope",
     "varlen_attention",
     "rope_attention",
+    "qkv_rope",
     "varlen_attention_rows",
     "attention_flops",
     "attention_bytes",
@@ -204,3 +208,16 @@ def attention_flops(cu_seqlens, heads: int, head_dim: int) -> int:
 def attention_bytes(total: int, nseg: int, heads: int, head_dim: int, cs_bytes: int = 4, io_bytes: int = 2) -> int:
     """Algorithmic bytes: Q, K, V read + O written, cos/sin read once, cu_seqlens."""
     return 4 * total * heads * head_dim * io_bytes + 2 * total * (head_dim // 2) * cs_bytes + 4 * (nseg + 1)
+
+
+def qkv_rope(x, w, b, cos, sin, heads: int, round_dtype: str | None = "bfloat16") -> np.ndarray:
+    """[T, 3, H, D]: qkv = x w^T + b (fp32 math) rounded to ``round_dtype``, then q, k
+    rotated with apply_rope (fp32, rounded again) and v as projected (bench.py:72-78)."""
+    T = x.shape[0]
+    y = x.astype(np.float32) @ w.astype(np.float32).T
+    if b is not None:
+        y = y + b.astype(np.float32)
+    y = round_to(y.astype(np.float32), round_dtype).reshape(T, 3, heads, -1)
+    q = apply_rope(y[:, 0], cos, sin, round_dtype)
+    k = apply_rope(y[:, 1], cos, sin, round_dtype)
+    return np.stack([q, k, y[:, 2]], axis=1)
