@@ -370,6 +370,87 @@ def projection_timing(torch, dev, peak_tflops, reps=50):
     return res
 
 
+def backward_timing(torch, dev, peak_tflops, reps=20):
+    """Backward pass (frattn_bwd) on the config-2 layers (896x896: one 4096-token
+    segment, and 64 windows of 64), CUDA-graph replay, CUDA events. FLOPs counted as
+    2.5x the forward's 4 sum(L^2) H D (S recomputed, dP, dV, dK, dQ). Comparator:
+    autograd through separate RoPE + flash_attn_varlen_func (its backward)."""
+    from fused_rope_attn_b200 import fused_attn as FA
+    from fused_rope_attn_b200.encoder import rope_unfused
+    from fused_rope_attn_b200.utils import get_window_index, segments_per_image
+    from fused_rope_attn_b200 import compute_rope_2d
+    res = {}
+    grid = [(1, 64, 64)]
+    H, D = 16, 80
+    for var in ("full", "windowed"):
+        if var == "full":
+            cu = segments_per_image(grid)
+            cos, sin = compute_rope_2d(grid, D, 2, 10000.0, dev, torch.float32)
+            hint = 4096
+        else:
+            widx, cu = get_window_index(grid)
+            cos, sin = compute_rope_2d(grid, D, 2, 10000.0, dev, torch.float32, window_idx=widx)
+            hint = 64
+        cu = cu.to(dev)
+        T = int(cu[-1])
+        g = torch.Generator(device=dev).manual_seed(1)
+        q, k, v, dout = (torch.randn(T, H, D, generator=g, device=dev).to(torch.bfloat16) for _ in range(4))
+        out, lse = FA._fwd_lse(q, k, v, cos, sin, cu, hint)
+        fwd_flop = 4.0 * sum((b - a) ** 2 for a, b in zip(cu.tolist()[:-1], cu.tolist()[1:])) * H * D
+
+        def ours():
+            FA._bwd(q, k, v, cos, sin, cu, out, lse, dout)
+
+        def timed(fn):
+            s = torch.cuda.Stream(device=dev)
+            with torch.cuda.stream(s):
+                for _ in range(3):
+                    fn()
+            torch.cuda.synchronize(dev)
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=s):
+                fn()
+            gr.replay()
+            torch.cuda.synchronize(dev)
+            a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(reps):
+                gr.replay()
+            e.record()
+            torch.cuda.synchronize(dev)
+            return a.elapsed_time(e) * 1e3 / reps
+
+        us = timed(ours)
+        row = {"tokens": T, "segments": cu.numel() - 1, "ours_us": us, "bwd_tflop": 2.5 * fwd_flop / 1e12,
+               "ours_tflops": 2.5 * fwd_flop / (us * 1e-6) / 1e12}
+        row["ours_frac_of_bf16_peak"] = row["ours_tflops"] / peak_tflops
+        try:
+            from flash_attn import flash_attn_varlen_func
+            qg, kg, vg = (t.clone().requires_grad_(True) for t in (q, k, v))
+            o = flash_attn_varlen_func(rope_unfused(qg, cos, sin), rope_unfused(kg, cos, sin), vg, cu, cu, hint, hint,
+                                       0.0, D ** -0.5, False)
+
+            def fa_bwd():
+                torch.autograd.grad(o, (qg, kg, vg), dout, retain_graph=True)
+
+            for _ in range(3):
+                fa_bwd()
+            torch.cuda.synchronize(dev)
+            a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(reps):
+                fa_bwd()
+            e.record()
+            torch.cuda.synchronize(dev)
+            row["rope_plus_fa2_bwd_us"] = a.elapsed_time(e) * 1e3 / reps
+            row["speedup_vs_rope_plus_fa2_bwd"] = row["rope_plus_fa2_bwd_us"] / us
+        except Exception as exc:  # noqa: BLE001 - comparator only
+            row["rope_plus_fa2_bwd_us"] = f"unavailable: {type(exc).__name__}: {exc}"[:200]
+        res[var] = row
+    res["kernels"] = "bwd_prep (rotate q/k, rowsum(dO o O)), bwd_main (tcgen05, per 128-key chunk), bwd_dq"
+    return res
+
+
 # --------------------------------------------------------------------------- config 5
 DP_GRIDS = [(1, 64, 64)] * 64 + [(8, 32, 32)] * 8  # 64 images 896x896 + 8 clips (16 frames 448x448, t=8)
 
@@ -707,6 +788,10 @@ def run_ours(args):
             except Exception as exc:  # noqa: BLE001
                 line["gpu_comparators"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
         if not args.no_encoder:
+            try:
+                line["backward"] = backward_timing(torch, dev, tflops)
+            except Exception as exc:  # noqa: BLE001
+                line["backward"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
             try:
                 line["qkv_projection"] = projection_timing(torch, dev, tflops)
             except Exception as exc:  # noqa: BLE001

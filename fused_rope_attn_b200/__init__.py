@@ -10,6 +10,7 @@ from .fused_attn import (  # noqa: F401
     fused_attention_rotated,
     fused_rope_attention,
     fused_rope_attention_pos,
+    fused_rope_attention_train,
     last_status,
     next_pow2,
     qkv_rope_projection,

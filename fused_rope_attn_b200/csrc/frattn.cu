@@ -200,7 +200,7 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
              const int32_t* cu, int nseg, int T, int H, int D, int in_dtype, void* out,
              void* workspace, size_t ws_bytes, int32_t* status, void* stream,
              int max_seqlen = 0, long long q_stride = 0, long long k_stride = 0,
-             long long v_stride = 0) {
+             long long v_stride = 0, float* lse = nullptr) {
   int rc = common_checks(q, k, v, cu, nseg, T, H, D, in_dtype, out, workspace);
   if (rc) return rc;
   // token strides of q, k, v in elements (0: contiguous [T, H, D]); TMA needs
@@ -284,6 +284,7 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
   prm.H = H;
   prm.status = status;
   prm.wait_limit_ns = g_wait_limit_ns;
+  prm.lse = lse;
   // Window regime (the caller says no segment exceeds one tile): one kernel,
   // no work list. Head dims / element types without a window kernel, and the
   // position entry point, take the general path below.
@@ -414,6 +415,17 @@ int frattn_fwd_pos(const void* q, const void* k, const void* v, const int32_t* p
   return fwd_impl<kRopePos>(q, k, v, nullptr, nullptr, FRATTN_F32, pos_hw, max_position, theta,
                             cu_seqlens, nseg, T, H, D, in_dtype, out, workspace, workspace_bytes,
                             status, stream, max_seqlen);
+}
+
+int frattn_fwd_lse(const void* q, const void* k, const void* v, const void* cos, const void* sin,
+                   int cs_dtype, const int32_t* cu_seqlens, int nseg, int T, int H, int D,
+                   int max_seqlen, int in_dtype, void* out, float* lse, void* workspace,
+                   size_t workspace_bytes, int32_t* status, void* stream) {
+  if (!lse) return FRATTN_E_NULL;
+  if (reinterpret_cast<uintptr_t>(lse) & 3u) return FRATTN_E_ALIGN;
+  return fwd_impl<kRopeTable>(q, k, v, cos, sin, cs_dtype, nullptr, 0, 0.f, cu_seqlens, nseg, T,
+                              H, D, in_dtype, out, workspace, workspace_bytes, status, stream,
+                              max_seqlen, 0, 0, 0, lse);
 }
 
 int frattn_fwd_rotated(const void* q, const void* k, const void* v, long long q_stride,

@@ -126,6 +126,7 @@ struct Params {
   int T, H;
   int32_t* status;
   unsigned long long wait_limit_ns;
+  float* lse;               // [T, H] base-2 log-sum-exp of the scaled scores, or nullptr
 };
 
 // ------------------------------------------------------------------ helpers
@@ -1159,6 +1160,9 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
       tc_fence_after();
       const bool store = lo < hi;
       const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
+      if (p.lse && row < q1x)  // log2 of the softmax denominator of the scaled scores
+        p.lse[static_cast<size_t>(row) * p.H + h] =
+            (store && l > 0.f) ? m_ref * sl2 + log2f(l) : -INFINITY;
       TI* orow = static_cast<TI*>(p.out) + (static_cast<size_t>(row) * p.H + h) * D;
       uint32_t oo[C::DP / 16][16];
 #pragma unroll
@@ -1915,6 +1919,9 @@ __global__ void __launch_bounds__(kWinThreads, 2) window_attn_kernel(const __gri
     TI* orow = static_cast<TI*>(p.out) + (static_cast<size_t>(min(row, p.T - 1)) * p.H + h) * D;
     const bool has = ok && lo < hi && l > 0.f;
     const float inv_l = has ? 1.f / l : 0.f;
+    if (p.lse && row < p.T)
+      p.lse[static_cast<size_t>(row) * p.H + h] =
+          has ? m_ref * (1.4426950408889634f * rsqrtf(static_cast<float>(D))) + log2f(l) : -INFINITY;
     uint32_t oo[C::DP / 16][16];
     if (nkv > 0) {
 #pragma unroll

@@ -505,3 +505,97 @@ def fused_attention_rotated(
         )
     _lib.check(rc, "frattn_fwd_rotated")
     return out
+
+
+# --------------------------------------------------------------------------- backward
+BACKWARD_HEAD_DIMS = (32, 48, 64, 80)
+
+
+def _fwd_lse(q, k, v, cos, sin, cu, max_seqlen):
+    """Forward that also returns lse [T, H] (fp32, base-2 log-sum-exp of the scaled scores)."""
+    total, heads, hd = (int(x) for x in q.shape)
+    out = torch.empty_like(q)
+    lse = torch.empty(total, heads, dtype=torch.float32, device=q.device)
+    nseg = cu.numel() - 1
+    lib = _lib.load()
+    ws_bytes = _lib.workspace_bytes(total, nseg)
+    if not (max_seqlen and 0 < max_seqlen <= 128):
+        ws_bytes += _lib.workspace_bytes_rotated_k(total, heads, hd)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    with torch.cuda.device(q.device):
+        rc = lib.frattn_fwd_lse(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), cos.data_ptr(), sin.data_ptr(), _DT[cos.dtype], cu.data_ptr(),
+            nseg, total, heads, hd, int(max_seqlen or 0), _DT[q.dtype], out.data_ptr(), lse.data_ptr(),
+            ws.data_ptr(), ws_bytes, _status_word(q.device).data_ptr(), torch.cuda.current_stream(q.device).cuda_stream,
+        )
+    _lib.check(rc, "frattn_fwd_lse")
+    return out, lse
+
+
+def _bwd(q, k, v, cos, sin, cu, out, lse, dout):
+    total, heads, hd = (int(x) for x in q.shape)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    if total == 0:
+        return dq, dk, dv
+    dout = _aligned(dout.contiguous())
+    ws_bytes = _lib.workspace_bytes_bwd(total, heads, hd)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        rc = lib.frattn_bwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), cos.data_ptr(), sin.data_ptr(), _DT[cos.dtype], cu.data_ptr(),
+            cu.numel() - 1, total, heads, hd, _DT[q.dtype], out.data_ptr(), dout.data_ptr(), lse.data_ptr(),
+            dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), ws_bytes, _status_word(q.device).data_ptr(),
+            torch.cuda.current_stream(q.device).cuda_stream,
+        )
+    _lib.check(rc, "frattn_bwd")
+    return dq, dk, dv
+
+
+class _FusedRopeAttention(torch.autograd.Function):
+    """Autograd node of ``fused_rope_attention``: the forward saves lse, the
+    backward runs the sm_100a backward kernels (frattn_bwd). No gradient flows
+    to cos/sin or cu_seqlens."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, cos, sin, cu, max_seqlen):
+        out, lse = _fwd_lse(q, k, v, cos, sin, cu, max_seqlen)
+        ctx.save_for_backward(q, k, v, cos, sin, cu, out, lse)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, cos, sin, cu, out, lse = ctx.saved_tensors
+        dq, dk, dv = _bwd(q, k, v, cos, sin, cu, out, lse, dout)
+        return dq, dk, dv, None, None, None, None
+
+
+def fused_rope_attention_train(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    cu_seqlens: torch.Tensor,
+    *,
+    max_seqlen: int | None = None,
+) -> torch.Tensor:
+    """``fused_rope_attention`` with gradients for q, k and v (head_dim in
+    ``BACKWARD_HEAD_DIMS``). The reference is forward-only; this is the same
+    forward recording an autograd node whose backward is the sm_100a backward pass."""
+    total, heads, hd = _check_qkv(q, k, v)
+    if hd not in BACKWARD_HEAD_DIMS:
+        raise ValueError(f"head_dim {hd} has no backward kernel ({BACKWARD_HEAD_DIMS})")
+    if cos.shape != (total, hd // 2) or sin.shape != (total, hd // 2):
+        raise ValueError(
+            f"cos/sin must be [total_seq, head_dim//2]={total, hd // 2}, got cos={tuple(cos.shape)} sin={tuple(sin.shape)}"
+        )
+    if cos.dtype not in _DT or sin.dtype not in _DT:
+        raise ValueError(f"cos/sin dtype must be float16, bfloat16 or float32, got {cos.dtype} / {sin.dtype}")
+    if sin.dtype != cos.dtype:
+        sin = sin.to(cos.dtype)
+    q, k, v = (_aligned(t.contiguous()) for t in (q, k, v))
+    cos = _aligned(cos.to(q.device).contiguous()).detach()
+    sin = _aligned(sin.to(q.device).contiguous()).detach()
+    cu = _check_cu(cu_seqlens, q.device)
+    return _FusedRopeAttention.apply(q, k, v, cos, sin, cu, max_seqlen)

@@ -164,6 +164,33 @@ int frattn_fwd_rotated(const void* q, const void* k, const void* v, long long q_
                        int T, int H, int D, int max_seqlen, int in_dtype, void* out,
                        void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
 
+/* ---- Training (the reference is forward-only, fused_attn.py:246-423).
+ *
+ * frattn_fwd_lse: frattn_fwd that also writes lse [T, H] fp32, the base-2
+ * log-sum-exp of the scaled scores of each row and head
+ * (log2 sum_j 2^(s_ij log2(e) / sqrt(D)), s = R(q) R(k)^T); the backward pass
+ * recomputes the softmax from it. Values of rows outside every segment are
+ * unspecified.
+ *
+ * frattn_bwd: gradients of out = frattn_fwd(q, k, v, cos, sin, cu_seqlens) with
+ * respect to q, k and v, given dout [T, H, D], the forward's out and lse:
+ *   dv = P^T dout, dS = P o (dout v^T - rowsum(dout o out)),
+ *   dq = R^T(dS R(k)) / sqrt(D), dk = R^T(dS^T R(q)) / sqrt(D),
+ * P = softmax(R(q) R(k)^T / sqrt(D)) per segment and head, R^T the inverse
+ * rotation. cos/sin are constants (no gradient). Rows outside every segment
+ * get zero gradients. All tensors contiguous [T, H, D] (cos/sin [T, D/2]);
+ * D in {32, 48, 64, 80}; workspace >= frattn_workspace_bytes_bwd(T, H, D)
+ * bytes (rotated q and k, the row terms and an fp32 dq accumulator). */
+int frattn_fwd_lse(const void* q, const void* k, const void* v, const void* cos, const void* sin,
+                   int cs_dtype, const int32_t* cu_seqlens, int nseg, int T, int H, int D,
+                   int max_seqlen, int in_dtype, void* out, float* lse, void* workspace,
+                   size_t workspace_bytes, int32_t* status, void* stream);
+int frattn_workspace_bytes_bwd(int total_tokens, int num_heads, int head_dim, size_t* bytes);
+int frattn_bwd(const void* q, const void* k, const void* v, const void* cos, const void* sin,
+               int cs_dtype, const int32_t* cu_seqlens, int nseg, int T, int H, int D, int in_dtype,
+               const void* out, const void* dout, const float* lse, void* dq, void* dk, void* dv,
+               void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
 /* Allocation-free variant of frattn_fwd (no counterpart in the reference).
  *
  * For callers that cannot allocate device memory at the point of the call: a
