@@ -21,13 +21,14 @@
 //                   dV += P^T dO, dK += dS^T Q          (TS: P^T, dS^T from TMEM)
 //                   dQ_tile = dS K                      (SS: dS^T written to smem
 //                                                        as an MN-major A operand)
-//                 The 128 compute threads (one key row each) turn S^T, dP^T into
-//                 P^T and dS^T; the dQ tile (q rows = TMEM lanes) is added to the
-//                 fp32 accumulator with vector atomics. dK is scaled and inverse-
+//                 The 256 compute threads (one key row and half of the columns
+//                 each) turn S^T, dP^T into P^T and dS^T; the dQ tile (q rows =
+//                 TMEM lanes) is added to the fp32 [H, T, D] accumulator with
+//                 vector atomics, one row per lane. dK is scaled and inverse-
 //                 rotated in the epilogue; dV is stored as is.
 //   bwd_dq        one thread per (token, head): dq = R^T(dq_acc / sqrt(D))
-// Warp roles of bwd_main (192 threads): warp 0 TMA producer (K, V once; Q, dO
-// per q tile, two stages), warp 1 TMEM owner + MMA issuer, warps 2-5 compute.
+// Warp roles of bwd_main (320 threads): warp 0 TMA producer (K, V once; Q, dO
+// per q tile, two stages), warp 1 TMEM owner + MMA issuer, warps 2-9 compute.
 // Every mbarrier wait is bounded (status code, unwind, TMEM freed).
 #include "frattn_kernel.cuh"
 
@@ -41,7 +42,7 @@ struct BwdParams {
   int nseg, T, H;
   const float* lse;     // [T, H] base-2 log-sum-exp of the scaled scores (forward)
   const float* delta;   // [T, H] rowsum(dO o O)
-  float* dq_acc;        // [T, H, D] fp32
+  float* dq_acc;        // [H, T, D] fp32
   void* dk;             // [T, H, D]
   void* dv;
   const void* cos;      // [T, D/2]
@@ -158,7 +159,8 @@ __global__ void __launch_bounds__(256) bwd_prep(const TI* __restrict__ q, const 
     for (int e = 0; e < 8; ++e) acc = fmaf(a[e], b[e], acc);
   }
   delta[i] = acc;
-  float4* z = reinterpret_cast<float4*>(dq_acc + base);
+  const int hh = static_cast<int>(i % H);
+  float4* z = reinterpret_cast<float4*>(dq_acc + (static_cast<size_t>(hh) * T + t) * D);
 #pragma unroll
   for (int c = 0; c < D / 4; ++c) z[c] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
@@ -171,14 +173,15 @@ __global__ void __launch_bounds__(256) bwd_dq(const float* __restrict__ dq_acc, 
   if (i >= static_cast<long long>(T) * H) return;
   const int t = static_cast<int>(i / H);
   const size_t base = static_cast<size_t>(i) * D;
+  const size_t abase = (static_cast<size_t>(i % H) * T + t) * D;  // accumulator is [H, T, D]
   const float scale = rsqrtf(static_cast<float>(D));
 #pragma unroll 1
   for (int c = 0; c < D / 16; ++c) {
     float cs[8], sn[8];
     load8<TC>(cos + static_cast<size_t>(t) * (D / 2) + 8 * c, cs);
     load8<TC>(sin + static_cast<size_t>(t) * (D / 2) + 8 * c, sn);
-    const float4* a4 = reinterpret_cast<const float4*>(dq_acc + base + 8 * c);
-    const float4* b4 = reinterpret_cast<const float4*>(dq_acc + base + D / 2 + 8 * c);
+    const float4* a4 = reinterpret_cast<const float4*>(dq_acc + abase + 8 * c);
+    const float4* b4 = reinterpret_cast<const float4*>(dq_acc + abase + D / 2 + 8 * c);
     const float4 a0 = a4[0], a1 = a4[1], b0 = b4[0], b1 = b4[1];
     const float y0[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
     const float y1[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
@@ -198,8 +201,9 @@ __global__ void __launch_bounds__(256) bwd_dq(const float* __restrict__ dq_acc, 
 }
 
 // ------------------------------------------------------------------ main
+constexpr int kBwdThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 compute
 template <int D, typename TI, typename TC>
-__global__ void __launch_bounds__(192, 1) bwd_main(const __grid_constant__ BwdParams p) {
+__global__ void __launch_bounds__(kBwdThreads, 1) bwd_main(const __grid_constant__ BwdParams p) {
   using C = BwdCfg<D>;
   constexpr bool kBF16 = std::is_same<TI, __nv_bfloat16>::value;
   constexpr uint32_t SW32 = 6;
@@ -231,10 +235,14 @@ __global__ void __launch_bounds__(192, 1) bwd_main(const __grid_constant__ BwdPa
     qb = __ldg(p.cu + segment_of(p.cu, p.nseg, kl) + 1);
   }
   const int nq = (qb - qa + kTileM - 1) / kTileM;
+  // The key chunks of one segment visit its q tiles in rotated orders, so that
+  // their dQ additions land on different rows at any moment.
+  const int q_first = nq > 0 ? static_cast<int>(blockIdx.x) % nq : 0;
+  auto q_tile = [&](int i) { return qa + ((i + q_first) % nq) * kTileM; };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NBAR; ++i)
-      mbar_init(bar(i), (i == DS_READY || i == DQ_FREE || i >= VEC_READY) ? 128 : 1);
+      mbar_init(bar(i), (i == DS_READY || i == DQ_FREE || i >= VEC_READY) ? 256 : 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -261,7 +269,7 @@ __global__ void __launch_bounds__(192, 1) bwd_main(const __grid_constant__ BwdPa
         const int s = i & 1;
         if (!bwd_wait(bar(EMPTY + s), ((i >> 1) & 1) ^ 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x61))
           break;
-        const int q0 = qa + i * kTileM;
+        const int q0 = q_tile(i);
         mbar_arrive_expect_tx(bar(FULL + s), 2 * C::TILE);
 #pragma unroll
         for (int b = 0; b < C::KB; ++b) {
@@ -313,8 +321,9 @@ __global__ void __launch_bounds__(192, 1) bwd_main(const __grid_constant__ BwdPa
 #pragma unroll
         for (int kk = 0; kk < kTileN / 16; ++kk) {  // dV += P^T dO, dK += dS^T Q
           const uint64_t o = static_cast<uint64_t>((kk * 512) >> 4);
-          umma_ts(tmem + C::T_DV, tmem + C::T_S + kk * 8, do_mn + o, IDESC_TS, (i > 0 || kk > 0));
-          umma_ts(tmem + C::T_DK, tmem + C::T_DP + kk * 8, q_mn + o, IDESC_TS, (i > 0 || kk > 0));
+          const uint32_t acol = kk < 4 ? kk * 8 : 96 + (kk - 4) * 8;  // packed q columns 16 kk ..
+          umma_ts(tmem + C::T_DV, tmem + C::T_S + acol, do_mn + o, IDESC_TS, (i > 0 || kk > 0));
+          umma_ts(tmem + C::T_DK, tmem + C::T_DP + acol, q_mn + o, IDESC_TS, (i > 0 || kk > 0));
         }
 #pragma unroll
         for (int kk = 0; kk < kTileN / 16; ++kk) {  // dQ = dS K over the S columns (after dV read P^T)
@@ -331,7 +340,10 @@ __global__ void __launch_bounds__(192, 1) bwd_main(const __grid_constant__ BwdPa
     }
   } else {
     // -------------------------------------------------------------- compute
+    // 8 warps: warp w reads TMEM lane quarter w & 3 (rows t); the two warps of
+    // a quarter split the work by column halves (hf = 0, 1).
     const int t = ((warp & 3) << 5) | lane;  // TMEM lane: key row (S^T, dP^T, dV, dK), q row (dQ)
+    const int hf = (warp - 2) >> 2;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const int key = kc0 + t;
     int klo = 0, khi = 0;
@@ -343,19 +355,21 @@ __global__ void __launch_bounds__(192, 1) bwd_main(const __grid_constant__ BwdPa
       }
     }
     const float sl2 = 1.4426950408889634f * rsqrtf(static_cast<float>(D));
+    constexpr int DQH = D / 2;  // dQ columns per warp
+    float* dq_head = p.dq_acc + static_cast<size_t>(h) * p.T * D;                     // [T, D] of head h
     bool ok = true;
     for (int i = 0; i < nq && ok; ++i) {
       const int b = i & 1;
-      const int q0 = qa + i * kTileM;
+      const int q0 = q_tile(i);
       float* lsev = vec + b * 256;
       float* delv = lsev + 128;
       {
         const int q = q0 + t;
         const bool in = q < qb;
-        lsev[t] = in ? __ldg(p.lse + static_cast<size_t>(q) * p.H + h) : 0.f;
-        delv[t] = in ? __ldg(p.delta + static_cast<size_t>(q) * p.H + h) : 0.f;
+        const float* src = hf ? p.delta : p.lse;
+        (hf ? delv : lsev)[t] = in ? __ldg(src + static_cast<size_t>(q) * p.H + h) : 0.f;
       }
-      // (bounded barrier of the 128 compute threads: the tile's lse2 / delta are staged)
+      // (bounded barrier of the 256 compute threads: the tile's lse2 / delta are staged)
       mbar_arrive(bar(VEC_READY + b));
       ok = bwd_wait_warp(bar(VEC_READY + b), (i >> 1) & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x6A);
       if (ok) ok = bwd_wait_warp(bar(SD_FULL), i & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x66);
@@ -364,29 +378,40 @@ __global__ void __launch_bounds__(192, 1) bwd_main(const __grid_constant__ BwdPa
       if (!ok) break;
       tc_fence_after();
       const int lo_r = klo - q0, hi_r = khi - q0;  // valid q columns of this key row
+      // Packed P^T / dS^T of 32-column chunk c go to TMEM columns pcol(c) (16 wide).
+      // Half 0 (chunks 0, 1) writes columns 0..31, over S columns it has already
+      // read; half 1 (chunks 3, then 2) writes 96..127, over its own chunk 3. The
+      // two halves never write a column the other still has to read.
 #pragma unroll 1
-      for (int c = 0; c < kTileN / 32; ++c) {
+      for (int n = 0; n < 2; ++n) {
+        const int c = hf ? 3 - n : n;
+        const uint32_t pcol = hf ? 96u + 16u * (c - 2) : 16u * c;
         uint32_t sr[32], dr[32];
         tmem_ld32(lane_addr + C::T_S + 32 * c, sr);
         tmem_ld32(lane_addr + C::T_DP + 32 * c, dr);
         tmem_ld_wait();
         uint32_t pk[16], dk[16];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float pv[2], dv[2];
+        for (int e4 = 0; e4 < 32; e4 += 4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(lsev + 32 * c + e4);
+          const float4 d4 = *reinterpret_cast<const float4*>(delv + 32 * c + e4);
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dl[4] = {d4.x, d4.y, d4.z, d4.w};
+          float pv[4], dv[4];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int col = 32 * c + e + u;
+          for (int u = 0; u < 4; ++u) {
+            const int col = 32 * c + e4 + u;
             const bool valid = col >= lo_r && col < hi_r;
-            const float pe = valid ? ex2(__uint_as_float(sr[e + u]) * sl2 - lsev[col]) : 0.f;
+            const float pe = valid ? ex2(__uint_as_float(sr[e4 + u]) * sl2 - lv[u]) : 0.f;
             pv[u] = pe;
-            dv[u] = pe * (__uint_as_float(dr[e + u]) - delv[col]);
+            dv[u] = pe * (__uint_as_float(dr[e4 + u]) - dl[u]);
           }
-          pk[e / 2] = pack2<TI>(pv[0], pv[1]);
-          dk[e / 2] = pack2<TI>(dv[0], dv[1]);
+          pk[e4 / 2] = pack2<TI>(pv[0], pv[1]);
+          pk[e4 / 2 + 1] = pack2<TI>(pv[2], pv[3]);
+          dk[e4 / 2] = pack2<TI>(dv[0], dv[1]);
+          dk[e4 / 2 + 1] = pack2<TI>(dv[2], dv[3]);
         }
-        tmem_st16(lane_addr + C::T_S + 16 * c, pk);
-        tmem_st16(lane_addr + C::T_DP + 16 * c, dk);
+        tmem_st16(lane_addr + C::T_S + pcol, pk);
+        tmem_st16(lane_addr + C::T_DP + pcol, dk);
         // dS^T row t, q columns [32c, 32c + 32): chunks 4c .. 4c + 3 of the MN-major operand
         uint8_t* ds = smem + C::OFF_DS;
 #pragma unroll
@@ -398,81 +423,92 @@ __global__ void __launch_bounds__(192, 1) bwd_main(const __grid_constant__ BwdPa
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(bar(DS_READY));
-      // dQ tile (TMEM lane = q row) into the fp32 accumulator
+      // dQ tile (TMEM lane = q row): this warp's 32 rows x D/2 columns are added
+      // to the fp32 [T, D] accumulator rows of head h with vector atomics
       ok = bwd_wait_warp(bar(DQ_FULL), i & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x68);
       if (!ok) break;
       tc_fence_after();
       {
-        uint32_t dq[D];
+        uint32_t dq[DQH];
+        if constexpr (DQH % 16 == 0) {
 #pragma unroll
-        for (int c = 0; c < D / 16; ++c)
-          tmem_ld16(lane_addr + C::T_DQ + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(&dq[16 * c]));
+          for (int c = 0; c < DQH / 16; ++c)
+            tmem_ld16(lane_addr + C::T_DQ + hf * DQH + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(&dq[16 * c]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < DQH / 8; ++c)
+            tmem_ld8(lane_addr + C::T_DQ + hf * DQH + 8 * c, *reinterpret_cast<uint32_t(*)[8]>(&dq[8 * c]));
+        }
         tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(bar(DQ_FREE));  // the S columns may take the next S^T
+        // one row per lane: the 32 lanes of an atomic instruction hit 32
+        // different cache lines (same-line vector atomics serialise in L2)
         const int q = q0 + t;
         if (q < qb) {
-          float4* dst = reinterpret_cast<float4*>(p.dq_acc + (static_cast<size_t>(q) * p.H + h) * D);
+          float4* dst = reinterpret_cast<float4*>(dq_head + static_cast<size_t>(q) * D + hf * DQH);
 #pragma unroll
-          for (int c = 0; c < D / 4; ++c)
+          for (int c = 0; c < DQH / 4; ++c)
             atomicAdd(dst + c, make_float4(__uint_as_float(dq[4 * c]), __uint_as_float(dq[4 * c + 1]),
                                            __uint_as_float(dq[4 * c + 2]), __uint_as_float(dq[4 * c + 3])));
         }
       }
-      tc_fence_before();
-      mbar_arrive(bar(DQ_FREE));
     }
-    // epilogue: dV as is, dK scaled and rotated back; keys outside every segment get 0
+    // epilogue: half 0 stores dV as is, half 1 stores dK scaled and rotated back;
+    // keys outside every segment get 0
     if (ok && nq > 0) ok = bwd_wait_warp(bar(ACC_FULL), 0, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x69);
     tc_fence_after();
-    uint32_t va[D], ka[D];
+    uint32_t acc[D];
     if (ok && nq > 0) {
 #pragma unroll
-      for (int c = 0; c < D / 16; ++c) {
-        tmem_ld16(lane_addr + C::T_DV + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(&va[16 * c]));
-        tmem_ld16(lane_addr + C::T_DK + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(&ka[16 * c]));
-      }
+      for (int c = 0; c < D / 16; ++c)
+        tmem_ld16(lane_addr + (hf ? C::T_DK : C::T_DV) + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(&acc[16 * c]));
       tmem_ld_wait();
     }
     if (key < kc1 && (ok || nq == 0)) {
       const bool has = nq > 0 && klo < khi;
       const size_t base = (static_cast<size_t>(key) * p.H + h) * D;
-      TI* dvp = static_cast<TI*>(p.dv) + base;
-      TI* dkp = static_cast<TI*>(p.dk) + base;
-      const float scale = rsqrtf(static_cast<float>(D));
-      const TC* cr = static_cast<const TC*>(p.cos) + static_cast<size_t>(key) * (D / 2);
-      const TC* sr = static_cast<const TC*>(p.sin) + static_cast<size_t>(key) * (D / 2);
+      if (hf == 0) {
+        TI* dvp = static_cast<TI*>(p.dv) + base;
 #pragma unroll
-      for (int c = 0; c < D / 8; ++c) {
-        uint4 w;
-        uint32_t* ww = reinterpret_cast<uint32_t*>(&w);
+        for (int c = 0; c < D / 8; ++c) {
+          uint4 w;
+          uint32_t* ww = reinterpret_cast<uint32_t*>(&w);
 #pragma unroll
-        for (int e = 0; e < 8; e += 2)
-          ww[e / 2] = pack2<TI>(has ? __uint_as_float(va[8 * c + e]) : 0.f,
-                                has ? __uint_as_float(va[8 * c + e + 1]) : 0.f);
-        *reinterpret_cast<uint4*>(dvp + 8 * c) = w;
-      }
-#pragma unroll
-      for (int c = 0; c < D / 16; ++c) {
-        float cs[8], sn[8];
-        load8<TC>(cr + 8 * c, cs);
-        load8<TC>(sr + 8 * c, sn);
-        uint4 oa, ob;
-        uint32_t* wa = reinterpret_cast<uint32_t*>(&oa);
-        uint32_t* wb = reinterpret_cast<uint32_t*>(&ob);
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          float a[2], bb[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const float y0 = has ? __uint_as_float(ka[8 * c + e + u]) * scale : 0.f;
-            const float y1 = has ? __uint_as_float(ka[D / 2 + 8 * c + e + u]) * scale : 0.f;
-            a[u] = y0 * cs[e + u] + y1 * sn[e + u];
-            bb[u] = y1 * cs[e + u] - y0 * sn[e + u];
-          }
-          wa[e / 2] = pack2<TI>(a[0], a[1]);
-          wb[e / 2] = pack2<TI>(bb[0], bb[1]);
+          for (int e = 0; e < 8; e += 2)
+            ww[e / 2] = pack2<TI>(has ? __uint_as_float(acc[8 * c + e]) : 0.f,
+                                  has ? __uint_as_float(acc[8 * c + e + 1]) : 0.f);
+          *reinterpret_cast<uint4*>(dvp + 8 * c) = w;
         }
-        *reinterpret_cast<uint4*>(dkp + 8 * c) = oa;
-        *reinterpret_cast<uint4*>(dkp + D / 2 + 8 * c) = ob;
+      } else {
+        TI* dkp = static_cast<TI*>(p.dk) + base;
+        const float scale = rsqrtf(static_cast<float>(D));
+        const TC* cr = static_cast<const TC*>(p.cos) + static_cast<size_t>(key) * (D / 2);
+        const TC* sr = static_cast<const TC*>(p.sin) + static_cast<size_t>(key) * (D / 2);
+#pragma unroll
+        for (int c = 0; c < D / 16; ++c) {
+          float cs[8], sn[8];
+          load8<TC>(cr + 8 * c, cs);
+          load8<TC>(sr + 8 * c, sn);
+          uint4 oa, ob;
+          uint32_t* wa = reinterpret_cast<uint32_t*>(&oa);
+          uint32_t* wb = reinterpret_cast<uint32_t*>(&ob);
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            float a[2], bb[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const float y0 = has ? __uint_as_float(acc[8 * c + e + u]) * scale : 0.f;
+              const float y1 = has ? __uint_as_float(acc[D / 2 + 8 * c + e + u]) * scale : 0.f;
+              a[u] = y0 * cs[e + u] + y1 * sn[e + u];
+              bb[u] = y1 * cs[e + u] - y0 * sn[e + u];
+            }
+            wa[e / 2] = pack2<TI>(a[0], a[1]);
+            wb[e / 2] = pack2<TI>(bb[0], bb[1]);
+          }
+          *reinterpret_cast<uint4*>(dkp + 8 * c) = oa;
+          *reinterpret_cast<uint4*>(dkp + D / 2 + 8 * c) = ob;
+        }
       }
     }
   }
@@ -574,7 +610,7 @@ static int launch_bwd(const void* q, const void* k, const void* v, const void* c
       return FRATTN_E_CUDA;
     attr_set |= bitv;
   }
-  kern<<<dim3((T + kTileM - 1) / kTileM, H), 192, C::SMEM, st>>>(p);
+  kern<<<dim3((T + kTileM - 1) / kTileM, H), kBwdThreads, C::SMEM, st>>>(p);
   if (cudaGetLastError() != cudaSuccess) return FRATTN_E_CUDA;
   bwd_dq<D, TI, TC><<<pb, 256, 0, st>>>(dq_acc, static_cast<const TC*>(cos), static_cast<const TC*>(sin), T, H,
                                         static_cast<TI*>(dq));
