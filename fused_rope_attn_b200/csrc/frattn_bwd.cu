@@ -41,7 +41,7 @@ struct BwdParams {
   const int32_t* cu;
   int nseg, T, H;
   const float* lse;     // [T, H] base-2 log-sum-exp of the scaled scores (forward)
-  const float* delta;   // [T, H] rowsum(dO o O)
+  const float* delta;   // [H, T] rowsum(dO o O)
   float* dq_acc;        // [H, T, D] fp32
   void* dk;             // [T, H, D]
   void* dv;
@@ -158,8 +158,8 @@ __global__ void __launch_bounds__(256) bwd_prep(const TI* __restrict__ q, const 
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc = fmaf(a[e], b[e], acc);
   }
-  delta[i] = acc;
   const int hh = static_cast<int>(i % H);
+  delta[static_cast<size_t>(hh) * T + t] = acc;  // [H, T]
   float4* z = reinterpret_cast<float4*>(dq_acc + (static_cast<size_t>(hh) * T + t) * D);
 #pragma unroll
   for (int c = 0; c < D / 4; ++c) z[c] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -201,6 +201,14 @@ __global__ void __launch_bounds__(256) bwd_dq(const float* __restrict__ dq_acc, 
 }
 
 // ------------------------------------------------------------------ main
+// Timeline trace (build with -DFRATTN_BWD_TRACE): SM clock stamps of CTA 0's
+// first 32 q tiles, read back with frattn_bwd_trace_read.
+#ifdef FRATTN_BWD_TRACE
+static __device__ unsigned long long g_bwd_trace[16 * 32];
+#define BT(ev, i) do { if (blockIdx.x == 0 && blockIdx.y == 0 && (i) < 32) g_bwd_trace[(ev) * 32 + (i)] = clock64(); } while (0)
+#else
+#define BT(ev, i) do { } while (0)
+#endif
 constexpr int kBwdThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 compute
 template <int D, typename TI, typename TC>
 __global__ void __launch_bounds__(kBwdThreads, 1) bwd_main(const __grid_constant__ BwdParams p) {
@@ -293,6 +301,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_main(const __grid_constant
       for (int i = 0; i < nq && ok; ++i) {
         const int s = i & 1;
         ok = bwd_wait(bar(FULL + s), (i >> 1) & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x63);
+        BT(0, i);
         if (!ok) break;
         tc_fence_after();
         const uint32_t qaddr = sbase + C::OFF_Q + s * C::TILE, doaddr = sbase + C::OFF_DO + s * C::TILE;
@@ -313,7 +322,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_main(const __grid_constant
           umma_ss(tmem + C::T_S, k_k + o, q_k + o, IDESC_SS, kb > 0);
         }
         umma_commit(bar(SD_FULL));
+        BT(1, i);
         ok = bwd_wait(bar(DS_READY), i & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x64);
+        BT(2, i);
         if (!ok) break;
         tc_fence_after();
         const uint64_t do_mn = make_sdesc(doaddr, kBlkBytes, 256, SW32);
@@ -331,6 +342,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_main(const __grid_constant
           umma_ss(tmem + C::T_DQ, ds_mn + o, k_mn + o, IDESC_DQ, kk > 0);
         }
         umma_commit(bar(DQ_FULL));
+        BT(3, i);
         umma_commit(bar(EMPTY + s));
         umma_commit(bar(DS_FREE));
       }
@@ -357,22 +369,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_main(const __grid_constant
     const float sl2 = 1.4426950408889634f * rsqrtf(static_cast<float>(D));
     constexpr int DQH = D / 2;  // dQ columns per warp
     float* dq_head = p.dq_acc + static_cast<size_t>(h) * p.T * D;                     // [T, D] of head h
+    // this thread's lse (half 0) or delta (half 1) value of row t of a q tile,
+    // loaded one tile ahead
+    auto row_term = [&](int q0) -> float {
+      const int q = q0 + t;
+      if (q >= qb) return 0.f;
+      return hf ? __ldg(p.delta + static_cast<size_t>(h) * p.T + q)
+                : __ldg(p.lse + static_cast<size_t>(q) * p.H + h);
+    };
+    float term = nq > 0 ? row_term(q_tile(0)) : 0.f;
     bool ok = true;
     for (int i = 0; i < nq && ok; ++i) {
       const int b = i & 1;
       const int q0 = q_tile(i);
       float* lsev = vec + b * 256;
       float* delv = lsev + 128;
-      {
-        const int q = q0 + t;
-        const bool in = q < qb;
-        const float* src = hf ? p.delta : p.lse;
-        (hf ? delv : lsev)[t] = in ? __ldg(src + static_cast<size_t>(q) * p.H + h) : 0.f;
-      }
+      (hf ? delv : lsev)[t] = term;
       // (bounded barrier of the 256 compute threads: the tile's lse2 / delta are staged)
       mbar_arrive(bar(VEC_READY + b));
       ok = bwd_wait_warp(bar(VEC_READY + b), (i >> 1) & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x6A);
+      if (t == 0 && hf == 0) BT(4, i);
       if (ok) ok = bwd_wait_warp(bar(SD_FULL), i & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x66);
+      if (t == 0 && hf == 0) BT(5, i);
       if (ok && i > 0)
         ok = bwd_wait_warp(bar(DS_FREE), (i - 1) & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x67);
       if (!ok) break;
@@ -423,9 +441,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_main(const __grid_constant
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(bar(DS_READY));
+      if (t == 0 && hf == 0) BT(6, i);
+      if (i + 1 < nq) term = row_term(q_tile(i + 1));  // latency hidden by the dQ phase
       // dQ tile (TMEM lane = q row): this warp's 32 rows x D/2 columns are added
       // to the fp32 [T, D] accumulator rows of head h with vector atomics
       ok = bwd_wait_warp(bar(DQ_FULL), i & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x68);
+      if (t == 0 && hf == 0) BT(7, i);
       if (!ok) break;
       tc_fence_after();
       {
@@ -442,8 +463,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_main(const __grid_constant
         tmem_ld_wait();
         tc_fence_before();
         mbar_arrive(bar(DQ_FREE));  // the S columns may take the next S^T
-        // one row per lane: the 32 lanes of an atomic instruction hit 32
-        // different cache lines (same-line vector atomics serialise in L2)
+        if (t == 0 && hf == 0) BT(8, i);
+        // One row per lane: the 32 lanes of an atomic instruction hit 32
+        // different cache lines (same-line vector atomics serialise in L2; a
+        // staged bulk reduce-add of the contiguous tile measured slower, its
+        // shared-memory reads drain at a few bytes per clock).
         const int q = q0 + t;
         if (q < qb) {
           float4* dst = reinterpret_cast<float4*>(dq_head + static_cast<size_t>(q) * D + hf * DQH);
@@ -452,6 +476,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_main(const __grid_constant
             atomicAdd(dst + c, make_float4(__uint_as_float(dq[4 * c]), __uint_as_float(dq[4 * c + 1]),
                                            __uint_as_float(dq[4 * c + 2]), __uint_as_float(dq[4 * c + 3])));
         }
+        if (t == 0 && hf == 0) BT(9, i);
       }
     }
     // epilogue: half 0 stores dV as is, half 1 stores dK scaled and rotated back;
@@ -686,3 +711,10 @@ extern "C" int frattn_bwd(const void* q, const void* k, const void* v, const voi
     default: return FRATTN_E_SHAPE;
   }
 }
+
+#ifdef FRATTN_BWD_TRACE
+extern "C" int frattn_bwd_trace_read(unsigned long long* host, int words) {
+  if (words > 16 * 32) words = 16 * 32;
+  return cudaMemcpyFromSymbol(host, frattn::g_bwd_trace, words * sizeof(unsigned long long)) == cudaSuccess ? 0 : 1;
+}
+#endif
