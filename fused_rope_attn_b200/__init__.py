@@ -9,6 +9,7 @@ from .fused_attn import (  # noqa: F401
     compute_rope_2d,
     fused_attention_rotated,
     fused_rope_attention,
+    fused_rope_attention_fp8,
     fused_rope_attention_pos,
     fused_rope_attention_train,
     last_status,

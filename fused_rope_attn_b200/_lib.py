@@ -42,6 +42,8 @@ _SIGNATURES = {
     "frattn_workspace_bytes_bwd": (_i, [_i, _i, _i, ctypes.POINTER(_sz)]),
     "frattn_bwd": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
                        _vp, _vp]),
+    "frattn_workspace_bytes_fp8": (_i, [_i, _i, _i, _i, ctypes.POINTER(_sz)]),
+    "frattn_fwd_fp8": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _sz, _vp, _vp]),
     "frattn_fwd_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
     "frattn_window_plan_sizes": (_i, [_vp, _i, _i, _i, _i, ctypes.POINTER(ctypes.c_int64),
                                       ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(_sz)]),
@@ -130,4 +132,11 @@ def workspace_bytes_bwd(total_tokens: int, num_heads: int, head_dim: int) -> int
     out = ctypes.c_size_t(0)
     check(load().frattn_workspace_bytes_bwd(int(total_tokens), int(num_heads), int(head_dim), ctypes.byref(out)),
           "frattn_workspace_bytes_bwd")
+    return int(out.value)
+
+
+def workspace_bytes_fp8(total_tokens: int, num_segments: int, num_heads: int, head_dim: int) -> int:
+    out = ctypes.c_size_t(0)
+    check(load().frattn_workspace_bytes_fp8(int(total_tokens), int(num_segments), int(num_heads), int(head_dim),
+                                            ctypes.byref(out)), "frattn_workspace_bytes_fp8")
     return int(out.value)

@@ -24,7 +24,8 @@ INST_SRC = os.path.join(CSRC, "frattn_inst.cu")
 WINDOW_SRC = os.path.join(CSRC, "frattn_window.cu")
 QKV_SRC = os.path.join(CSRC, "frattn_qkv.cu")
 BWD_SRC = os.path.join(CSRC, "frattn_bwd.cu")
-DEPS = [HOST_SRC, INST_SRC, WINDOW_SRC, QKV_SRC, BWD_SRC, os.path.join(CSRC, "frattn_kernel.cuh"), os.path.join(CSRC, "frattn_ptx.cuh"),
+FP8_SRC = os.path.join(CSRC, "frattn_fp8.cu")
+DEPS = [HOST_SRC, INST_SRC, WINDOW_SRC, QKV_SRC, BWD_SRC, FP8_SRC, os.path.join(CSRC, "frattn_kernel.cuh"), os.path.join(CSRC, "frattn_ptx.cuh"),
         os.path.join(ROOT, "include", "frattn.h")]
 OUT = os.path.join(HERE, "libfrattn.so")
 OBJ_DIR = os.path.join(HERE, "_build")
@@ -73,6 +74,9 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -
     win_obj = os.path.join(OBJ_DIR, "frattn_window.o")
     cmds.append([nvcc(), *NVCC_FLAGS, *extra, "-c", "-o", win_obj, WINDOW_SRC])
     objs.append(win_obj)
+    fp8_obj = os.path.join(OBJ_DIR, "frattn_fp8.o")
+    cmds.append([nvcc(), *NVCC_FLAGS, *extra, "-c", "-o", fp8_obj, FP8_SRC])
+    objs.append(fp8_obj)
     bwd_obj = os.path.join(OBJ_DIR, "frattn_bwd.o")
     cmds.append([nvcc(), *NVCC_FLAGS, *extra, "-c", "-o", bwd_obj, BWD_SRC])
     objs.append(bwd_obj)

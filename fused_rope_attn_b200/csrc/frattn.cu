@@ -74,11 +74,20 @@ thread_local cudaEvent_t g_ev_start = nullptr, g_ev_stop = nullptr;
 
 // (external records: during stream capture they become event-record nodes
 // whose timestamps the host can read after a replay)
+// (outside a capture the external flag is not accepted: plain records there)
+void timing_record(cudaEvent_t ev, cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(st, &cs);
+  if (cs == cudaStreamCaptureStatusActive)
+    cudaEventRecordWithFlags(ev, st, cudaEventRecordExternal);
+  else
+    cudaEventRecord(ev, st);
+}
 void timing_begin(cudaStream_t st) {
-  if (g_ev_start) cudaEventRecordWithFlags(g_ev_start, st, cudaEventRecordExternal);
+  if (g_ev_start) timing_record(g_ev_start, st);
 }
 void timing_end(cudaStream_t st) {
-  if (g_ev_stop) cudaEventRecordWithFlags(g_ev_stop, st, cudaEventRecordExternal);
+  if (g_ev_stop) timing_record(g_ev_stop, st);
   g_ev_start = g_ev_stop = nullptr;
 }
 
@@ -114,6 +123,21 @@ int make_cs_map(CUtensorMap* m, const void* base, int T, int D, int cs_dtype) {
   CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : FRATTN_E_TMAP;
+}
+
+// [T, H, D16] e4m3 rows (D16 bytes per head, zero-padded) viewed as 3-D {D16, H, T};
+// box {32, 1, 128} (32 e4m3 = 32 bytes per column block), 32-B swizzle.
+int make_fp8_map(CUtensorMap* m, const void* base, int T, int H, int D16) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (!enc) return FRATTN_E_TMAP;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D16), static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(T)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D16), static_cast<cuuint64_t>(H) * D16};
+  cuuint32_t box[3] = {32, 1, static_cast<cuuint32_t>(kTileM)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : FRATTN_E_TMAP;
 }
 
@@ -200,7 +224,8 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
              const int32_t* cu, int nseg, int T, int H, int D, int in_dtype, void* out,
              void* workspace, size_t ws_bytes, int32_t* status, void* stream,
              int max_seqlen = 0, long long q_stride = 0, long long k_stride = 0,
-             long long v_stride = 0, float* lse = nullptr) {
+             long long v_stride = 0, float* lse = nullptr, const float* qscale = nullptr,
+             const float* kscale = nullptr) {
   int rc = common_checks(q, k, v, cu, nseg, T, H, D, in_dtype, out, workspace);
   if (rc) return rc;
   // token strides of q, k, v in elements (0: contiguous [T, H, D]); TMA needs
@@ -209,8 +234,10 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
   if (q_stride == 0) q_stride = hd;
   if (k_stride == 0) k_stride = hd;
   if (v_stride == 0) v_stride = hd;
-  if (q_stride < hd || k_stride < hd || v_stride < hd) return FRATTN_E_SHAPE;
-  if ((q_stride | k_stride | v_stride) & 7) return FRATTN_E_ALIGN;
+  if (MODE != kRopeFp8) {  // (FP8: q_stride / k_stride carry the padded e4m3 head width)
+    if (q_stride < hd || k_stride < hd || v_stride < hd) return FRATTN_E_SHAPE;
+    if ((q_stride | k_stride | v_stride) & 7) return FRATTN_E_ALIGN;
+  }
   size_t need = 0;
   if (MODE == kRopeTable) {
     frattn_workspace_bytes(T, nseg, &need);
@@ -218,7 +245,7 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
     if (cs_dtype != FRATTN_F32 && cs_dtype != FRATTN_F16 && cs_dtype != FRATTN_BF16)
       return FRATTN_E_DTYPE;
     if (!aligned16(cos) || !aligned16(sin)) return FRATTN_E_ALIGN;
-  } else if (MODE == kRopeNone) {
+  } else if (MODE == kRopeNone || MODE == kRopeFp8) {
     frattn_workspace_bytes(T, nseg, &need);
   } else {
     if (!pos_hw) return FRATTN_E_NULL;
@@ -245,10 +272,16 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
   Params prm;
   memset(&prm, 0, sizeof(prm));
   const bool bf16 = in_dtype == FRATTN_BF16;
-  if (make_qkv_map(&prm.tmq, q, T, H, D, bf16, q_stride) ||
-      make_qkv_map(&prm.tmk, k, T, H, D, bf16, k_stride) ||
-      make_qkv_map(&prm.tmv, v, T, H, D, bf16, v_stride))
+  if (MODE == kRopeFp8) {  // q, k: e4m3 rows of q_stride bytes per head (the padded head dim)
+    if (make_fp8_map(&prm.tmq, q, T, H, static_cast<int>(q_stride)) ||
+        make_fp8_map(&prm.tmk, k, T, H, static_cast<int>(k_stride)) ||
+        make_qkv_map(&prm.tmv, v, T, H, D, bf16, v_stride))
+      return FRATTN_E_TMAP;
+  } else if (make_qkv_map(&prm.tmq, q, T, H, D, bf16, q_stride) ||
+             make_qkv_map(&prm.tmk, k, T, H, D, bf16, k_stride) ||
+             make_qkv_map(&prm.tmv, v, T, H, D, bf16, v_stride)) {
     return FRATTN_E_TMAP;
+  }
   // Rotated-K buffer after the work list (and table) when the workspace has
   // room. A caller's max_seqlen <= one tile says no segment is long, so the
   // pre-rotation pass would find nothing to do and is not launched. The hint
@@ -257,7 +290,7 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
   const size_t krot_off = (need + 255) & ~size_t(255);
   const size_t krot_bytes = static_cast<size_t>(T) * H * D * 2;
   const bool no_long = max_seqlen > 0 && max_seqlen <= kTileM;
-  if (MODE != kRopeNone && ws_bytes >= krot_off + krot_bytes && !no_long) {
+  if (MODE != kRopeNone && MODE != kRopeFp8 && ws_bytes >= krot_off + krot_bytes && !no_long) {
     prm.krot = ws + krot_off;
     if (make_qkv_map(&prm.tmk_rot, prm.krot, T, H, D, bf16, static_cast<long long>(H) * D))
       return FRATTN_E_TMAP;
@@ -285,10 +318,12 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
   prm.status = status;
   prm.wait_limit_ns = g_wait_limit_ns;
   prm.lse = lse;
+  prm.qscale = qscale;
+  prm.kscale = kscale;
   // Window regime (the caller says no segment exceeds one tile): one kernel,
   // no work list. Head dims / element types without a window kernel, and the
   // position entry point, take the general path below.
-  if (MODE != kRopePos && no_long) {
+  if ((MODE == kRopeTable || MODE == kRopeNone) && no_long) {
     timing_begin(st);  // the window kernel is then the only launch of the call
     rc = dispatch_window(prm, D, in_dtype, cs_dtype, MODE == kRopeNone, st);
     if (rc != FRATTN_E_SHAPE) {
@@ -310,6 +345,18 @@ int fwd_impl(const void* q, const void* k, const void* v, const void* cos, const
 namespace frattn {
 // Bounded-wait limit shared by every kernel of the library (frattn_set_wait_limit_ns).
 unsigned long long frattn_wait_limit_ns() { return g_wait_limit_ns; }
+
+// Attention over q / k already rotated and quantised to e4m3 (frattn_fp8.cu):
+// rows of D16 bytes per head, dequantisation scales per q row and per k head.
+int attn_fp8_prequantized(const void* q8, const void* k8, const void* v, const float* qscale,
+                          const float* kscale, int D16, const int32_t* cu, int nseg, int T, int H, int D,
+                          int in_dtype, void* out, void* workspace, size_t ws_bytes, int32_t* status,
+                          cudaStream_t st) {
+  if (!qscale || !kscale) return FRATTN_E_NULL;
+  return fwd_impl<kRopeFp8>(q8, k8, v, nullptr, nullptr, FRATTN_F32, nullptr, 0, 0.f, cu, nseg, T, H, D,
+                            in_dtype, out, workspace, ws_bytes, status, st, 0, D16, D16, 0, nullptr, qscale,
+                            kscale);
+}
 }  // namespace frattn
 
 // ---------------------------------------------------------------- no-alloc variant

@@ -20,6 +20,7 @@ int FRATTN_CAT(attn_d, FRATTN_D)(const Params& prm, int mode, int in_dtype, int 
 #else
   if (mode == kRopePos) return dispatch_in<FRATTN_D, kRopePos>(prm, in_dtype, cs_dtype, st);
   if (mode == kRopeNone) return dispatch_in<FRATTN_D, kRopeNone>(prm, in_dtype, cs_dtype, st);
+  if (mode == kRopeFp8) return dispatch_in<FRATTN_D, kRopeFp8>(prm, in_dtype, cs_dtype, st);
   return dispatch_in<FRATTN_D, kRopeTable>(prm, in_dtype, cs_dtype, st);
 #endif
 }

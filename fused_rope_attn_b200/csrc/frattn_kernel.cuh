@@ -104,7 +104,9 @@ __host__ __device__ inline size_t max_items(int T) {
 
 // Rotary angle source: materialised tables (reference API), (h, w) ids, or
 // none (q and k arrive rotated, e.g. from the QKV projection's epilogue).
-enum RopeMode : int { kRopeTable = 0, kRopePos = 1, kRopeNone = 2 };
+// kRopeFp8: q and k arrive rotated and quantised to e4m3 (per-row q scales,
+// per-head k scales); S = Q K^T runs as an FP8 MMA, P V stays 16-bit.
+enum RopeMode : int { kRopeTable = 0, kRopePos = 1, kRopeNone = 2, kRopeFp8 = 3 };
 
 struct Params {
   CUtensorMap tmq, tmk, tmv;
@@ -127,6 +129,8 @@ struct Params {
   int32_t* status;
   unsigned long long wait_limit_ns;
   float* lse;               // [T, H] base-2 log-sum-exp of the scaled scores, or nullptr
+  const float* qscale;      // [T, H] e4m3 dequantisation scales of q rows (kRopeFp8)
+  const float* kscale;      // [H] e4m3 dequantisation scale of k (kRopeFp8)
 };
 
 // ------------------------------------------------------------------ helpers
@@ -461,7 +465,7 @@ __device__ __forceinline__ void rope_row_elementwise(uint8_t* tile, int row0, co
 template <int D, int MODE, typename TI, typename TC>
 __device__ __forceinline__ void rope_tile(uint8_t* tile, int row0, const Params& p, int r0,
                                           const uint8_t* cs_smem = nullptr) {
-  if constexpr (MODE == kRopeNone) {
+  if constexpr (MODE == kRopeNone || MODE == kRopeFp8) {
     return;  // already rotated
   } else if constexpr (D % 16 == 0) {
     // One chunk pair per iteration, as a real loop: the rotation shares the
@@ -642,7 +646,7 @@ __device__ __forceinline__ Unit decode_unit(const Params& p, int u, int n_long) 
   return U;
 }
 
-template <int D, int CSB>
+template <int D, int CSB, bool FP8 = false>
 struct Cfg {
   static_assert(D % 8 == 0 && D >= 32 && D <= 128, "D must be a multiple of 8 in [32,128]");
   static constexpr int DP = (D + 15) / 16 * 16;      // tile width: D rounded up to the MMA K step
@@ -672,7 +676,9 @@ struct Cfg {
   // Rotated Q of slot X lives in TMEM behind O_X (columns DP .. DP + DP/2 of
   // the 128-column O region) when it fits; S then takes its A operand from
   // TMEM and the rotation never writes shared memory.
-  static constexpr bool Q_TMEM = (D % 16 == 0) && (DP + DP / 2 <= 128);
+  static constexpr bool Q_TMEM = !FP8 && (D % 16 == 0) && (DP + DP / 2 <= 128);
+  // FP8 q / k tiles: 32-element (32-byte) column blocks, zero-filled past D
+  static constexpr int KB8 = (D + 31) / 32;
   static constexpr uint32_t TMEM_Q = TMEM_O + DP;
 };
 
@@ -707,7 +713,10 @@ static_assert(128 * (REG_CTRL + REG_ROPE) + 256 * REG_SOFTMAX <= 512 * 128, "reg
 
 template <int D, int MODE, typename TI, typename TC>
 __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __grid_constant__ Params p) {
-  using C = Cfg<D, MODE == kRopeTable ? static_cast<int>(sizeof(TC)) : 0>;
+  using C = Cfg<D, MODE == kRopeTable ? static_cast<int>(sizeof(TC)) : 0, MODE == kRopeFp8>;
+  constexpr bool kFp8 = MODE == kRopeFp8;
+  constexpr uint32_t IDESC_S8 = make_idesc_f16(false, kTileM, kTileN, false);  // e4m3 x e4m3 (format 0)
+  constexpr int QK_BYTES = kFp8 ? C::KB8 * kBlkBytes : C::TILE_BYTES;         // one q / k tile
   constexpr int ST = C::STAGES;
   constexpr int QB = C::QBUF;
   using B = Bars<ST, QB>;
@@ -811,10 +820,10 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
                             FRATTN_STATUS_WAIT_TIMEOUT | 0x00);
           if (!ok) break;
           const uint32_t fb = bar(B::Q_FULL + x * QB + qs);
-          mbar_arrive_expect_tx(fb, C::TILE_BYTES);
+          mbar_arrive_expect_tx(fb, QK_BYTES);
 #pragma unroll
-          for (int b = 0; b < C::KB; ++b)
-            tma_load_3d(sbase + qbuf(x, qs) + b * kBlkBytes, &p.tmq, fb, 16 * b, x ? U.hb : U.ha,
+          for (int b = 0; b < (kFp8 ? C::KB8 : C::KB); ++b)
+            tma_load_3d(sbase + qbuf(x, qs) + b * kBlkBytes, &p.tmq, fb, (kFp8 ? 32 : 16) * b, x ? U.hb : U.ha,
                         x ? U.q0b : U.q0a);
           ++q_it[x];
         }
@@ -832,11 +841,11 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
                               FRATTN_STATUS_WAIT_TIMEOUT | 0x01);
             if (!ok) break;
             FR_TRACE((u - (int)blockIdx.x) / (int)gridDim.x, 0, j * 2 + x);
-            mbar_arrive_expect_tx(bar(B::K_FULL + ks), C::TILE_BYTES);
+            mbar_arrive_expect_tx(bar(B::K_FULL + ks), QK_BYTES);
 #pragma unroll
-            for (int b = 0; b < C::KB; ++b)
+            for (int b = 0; b < (kFp8 ? C::KB8 : C::KB); ++b)
               tma_load_3d(sbase + C::OFF_K + ks * C::TILE_BYTES + b * kBlkBytes, kmap,
-                          bar(B::K_FULL + ks), 16 * b, hx, row);
+                          bar(B::K_FULL + ks), (kFp8 ? 32 : 16) * b, hx, row);
             ++k_it;
             const int vs = v_it % ST;
             ok = bounded_wait(bar(B::V_EMPTY + vs), ((v_it / ST) & 1) ^ 1, p, abort_flag,
@@ -916,14 +925,22 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
                 const uint32_t kaddr = sbase + C::OFF_K + (ki % ST) * C::TILE_BYTES;
                 const uint64_t qdesc = make_sdesc(qaddr, 16, 256, SW32);
                 const uint64_t kdesc = make_sdesc(kaddr, 16, 256, SW32);
+                if constexpr (kFp8) {
 #pragma unroll
-                for (int kb = 0; kb < C::KB; ++kb) {
-                  const uint64_t bd = kdesc + static_cast<uint64_t>((kb * kBlkBytes) >> 4);
-                  if constexpr (C::Q_TMEM) {
-                    umma_ts(s_col, tmem + C::TMEM_Q + 128u * x + kb * 8, bd, IDESC_S, kb > 0 ? 1u : 0u);
-                  } else {
-                    const uint64_t ad = qdesc + static_cast<uint64_t>((kb * kBlkBytes) >> 4);
-                    umma_ss(s_col, ad, bd, IDESC_S, kb > 0 ? 1u : 0u);
+                  for (int kb = 0; kb < C::KB8; ++kb) {  // K = 32 e4m3 elements per MMA
+                    const uint64_t o = static_cast<uint64_t>((kb * kBlkBytes) >> 4);
+                    umma_ss_f8(s_col, qdesc + o, kdesc + o, IDESC_S8, kb > 0 ? 1u : 0u);
+                  }
+                } else {
+#pragma unroll
+                  for (int kb = 0; kb < C::KB; ++kb) {
+                    const uint64_t bd = kdesc + static_cast<uint64_t>((kb * kBlkBytes) >> 4);
+                    if constexpr (C::Q_TMEM) {
+                      umma_ts(s_col, tmem + C::TMEM_Q + 128u * x + kb * 8, bd, IDESC_S, kb > 0 ? 1u : 0u);
+                    } else {
+                      const uint64_t ad = qdesc + static_cast<uint64_t>((kb * kBlkBytes) >> 4);
+                      umma_ss(s_col, ad, bd, IDESC_S, kb > 0 ? 1u : 0u);
+                    }
                   }
                 }
                 FR_TRACE(ui, 11, j * 2 + x);
@@ -1027,7 +1044,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const uint32_t s_addr = lane_addr + C::TMEM_S + 128u * x;
     const uint32_t o_addr = lane_addr + C::TMEM_O + 128u * x;
-    const float sl2 = 1.4426950408889634f * rsqrtf(static_cast<float>(D));
+    const float sl2_base = 1.4426950408889634f * rsqrtf(static_cast<float>(D));
     constexpr float kRescaleLog2 = 8.0f;  // move the reference max only when it grows by 2^8
     constexpr int kPolyOf8 = FRATTN_POLY_OF_8;
     uint32_t s_it = 0, o_it = 0;
@@ -1054,6 +1071,10 @@ __global__ void __launch_bounds__(kThreads, 1) fused_rope_attn_kernel(const __gr
         }
       }
       float m_ref = -INFINITY, l = 0.f;
+      // exponent factor of the raw scores (FP8: times the dequantisation scales)
+      float sl2 = sl2_base;
+      if constexpr (kFp8)
+        sl2 *= __ldg(p.qscale + static_cast<size_t>(min(row, p.T - 1)) * p.H + h) * __ldg(p.kscale + h);
       for (int j = 0; j < nkv; ++j) {
         ok = bounded_wait_warp(bar(B::S_FULL + x), s_it & 1, p, abort_flag,
                                FRATTN_STATUS_WAIT_TIMEOUT | 0x30);
@@ -1397,7 +1418,7 @@ inline int sm_count_for_current_device() {
 
 template <int D, int MODE, typename TI, typename TC>
 int launch_attn(const Params& prm, cudaStream_t st) {
-  using C = Cfg<D, MODE == kRopeTable ? static_cast<int>(sizeof(TC)) : 0>;
+  using C = Cfg<D, MODE == kRopeTable ? static_cast<int>(sizeof(TC)) : 0, MODE == kRopeFp8>;
   auto kern = fused_rope_attn_kernel<D, MODE, TI, TC>;
   // Per-device flag; setting the attribute twice is harmless, so races are benign.
   static unsigned long long attr_set = 0;
@@ -1418,11 +1439,11 @@ int launch_attn(const Params& prm, cudaStream_t st) {
   lc.stream = st;
   lc.attrs = &attr;
   lc.numAttrs = 1;
-  if (MODE != kRopeNone && prm.krot) {
+  if (MODE != kRopeNone && MODE != kRopeFp8 && prm.krot) {
     lc.gridDim = dim3(2 * grid);
     lc.blockDim = dim3(256);
     lc.dynamicSmemBytes = 0;
-    if constexpr (MODE != kRopeNone)
+    if constexpr (MODE != kRopeNone && MODE != kRopeFp8)
       if (cudaLaunchKernelEx(&lc, rotate_k_long<D, MODE, TI, TC>, prm) != cudaSuccess) return FRATTN_E_CUDA;
   }
   lc.gridDim = dim3(grid);
@@ -1434,18 +1455,21 @@ int launch_attn(const Params& prm, cudaStream_t st) {
 
 template <int D, int MODE, typename TI>
 int dispatch_cs(const Params& prm, int cs_dtype, cudaStream_t st) {
-  if constexpr (MODE != kRopeTable) return launch_attn<D, MODE, TI, float>(prm, st);
+  if constexpr (MODE != kRopeTable) {  // no tables are read: one instantiation
+    return launch_attn<D, MODE, TI, float>(prm, st);
+  } else {
 #ifdef FRATTN_FAST_BUILD  // experiment builds: fp32 tables only
-  if (cs_dtype != FRATTN_F32) return FRATTN_E_DTYPE;
-  return launch_attn<D, MODE, TI, float>(prm, st);
+    if (cs_dtype != FRATTN_F32) return FRATTN_E_DTYPE;
+    return launch_attn<D, MODE, TI, float>(prm, st);
 #else
-  switch (cs_dtype) {
-    case FRATTN_F32: return launch_attn<D, MODE, TI, float>(prm, st);
-    case FRATTN_BF16: return launch_attn<D, MODE, TI, __nv_bfloat16>(prm, st);
-    case FRATTN_F16: return launch_attn<D, MODE, TI, __half>(prm, st);
-    default: return FRATTN_E_DTYPE;
-  }
+    switch (cs_dtype) {
+      case FRATTN_F32: return launch_attn<D, MODE, TI, float>(prm, st);
+      case FRATTN_BF16: return launch_attn<D, MODE, TI, __nv_bfloat16>(prm, st);
+      case FRATTN_F16: return launch_attn<D, MODE, TI, __half>(prm, st);
+      default: return FRATTN_E_DTYPE;
+    }
 #endif
+  }
 }
 
 template <int D, int MODE>

@@ -15,6 +15,8 @@ window permutation.
 
 Attention implementations (``attn=``):
 * ``"fused"``    — ``fused_rope_attention`` (this repository's sm_100a kernel);
+* ``"fused_fp8"`` — ``fused_rope_attention`` on window layers and the FP8
+                   (e4m3 q/k) variant ``fused_rope_attention_fp8`` on full layers;
 * ``"fused_qkv"`` — the QKV projection with RoPE in its epilogue
                    (``qkv_rope_projection``, an own tcgen05 GEMM) followed by
                    ``fused_attention_rotated``: no rotation in attention;
@@ -30,7 +32,8 @@ from dataclasses import dataclass, field
 
 import torch
 
-from .fused_attn import compute_rope_2d, fused_attention_rotated, fused_rope_attention, qkv_rope_projection
+from .fused_attn import (compute_rope_2d, fused_attention_rotated, fused_rope_attention, fused_rope_attention_fp8,
+                         qkv_rope_projection)
 from .utils import get_window_index, segments_per_image, window_shuffle, window_unshuffle
 
 __all__ = ["EncoderConfig", "VisionEncoder", "encoder_inputs", "rope_unfused", "attention_fp32"]
@@ -194,7 +197,9 @@ class VisionEncoder(torch.nn.Module):
             q, k, v = qkv[:, 0], qkv[:, 1], qkv[:, 2]
             if attn == "fused_qkv":
                 o = fused_attention_rotated(q, k, v, cu, max_seqlen=max_len)
-            elif attn == "fused":
+            elif attn == "fused_fp8" and full:
+                o = fused_rope_attention_fp8(q, k, v, plan["cos"], plan["sin"], cu, max_seqlen=max_len)
+            elif attn in ("fused", "fused_fp8"):
                 o = fused_rope_attention(q, k, v, plan["cos"], plan["sin"], cu, max_seqlen=max_len)
             elif attn == "unfused":
                 o = _attn_unfused(q, k, v, plan["cos"], plan["sin"], cu, max_len)

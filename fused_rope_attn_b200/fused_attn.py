@@ -599,3 +599,55 @@ def fused_rope_attention_train(
     sin = _aligned(sin.to(q.device).contiguous()).detach()
     cu = _check_cu(cu_seqlens, q.device)
     return _FusedRopeAttention.apply(q, k, v, cos, sin, cu, max_seqlen)
+
+
+# --------------------------------------------------------------------------- FP8 q / k
+def fused_rope_attention_fp8(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    cu_seqlens: torch.Tensor,
+    *,
+    out: torch.Tensor | None = None,
+    max_seqlen: int | None = None,
+) -> torch.Tensor:
+    """``fused_rope_attention`` with R(q) R(k)^T on the FP8 tensor cores.
+
+    q and k are rotated and rounded to e4m3 once per call (a scale per q row and
+    per k head), P V stays in q's dtype. Same arguments and checks as
+    ``fused_rope_attention``; head_dim a multiple of 16 in [32, 128]. Meant for
+    long segments (full-attention layers).
+    """
+    total, heads, hd = _check_qkv(q, k, v)
+    if hd % 16 or not 32 <= hd <= 128:
+        raise ValueError(f"head_dim {hd} is not supported by the FP8 path (multiples of 16 in [32, 128])")
+    if cos.shape != (total, hd // 2) or sin.shape != (total, hd // 2):
+        raise ValueError(
+            f"cos/sin must be [total_seq, head_dim//2]={total, hd // 2}, got cos={tuple(cos.shape)} sin={tuple(sin.shape)}"
+        )
+    if cos.dtype not in _DT or sin.dtype not in _DT:
+        raise ValueError(f"cos/sin dtype must be float16, bfloat16 or float32, got {cos.dtype} / {sin.dtype}")
+    if sin.dtype != cos.dtype:
+        sin = sin.to(cos.dtype)
+    if cu_seqlens.ndim != 1 or cu_seqlens.numel() < 2:
+        raise ValueError(f"cu_seqlens must be 1D with length >= 2, got {tuple(cu_seqlens.shape)}")
+    q, k, v = (_aligned(t.contiguous()) for t in (q, k, v))
+    cos = _aligned(cos.to(q.device).contiguous())
+    sin = _aligned(sin.to(q.device).contiguous())
+    out = _check_out(out, q)
+    cu = _check_cu(cu_seqlens, q.device)
+    nseg = cu.numel() - 1
+    lib = _lib.load()
+    ws_bytes = _lib.workspace_bytes_fp8(total, nseg, heads, hd)
+    ws = torch.empty(ws_bytes + 256, dtype=torch.uint8, device=q.device)
+    off = (-ws.data_ptr()) % 256
+    with torch.cuda.device(q.device):
+        rc = lib.frattn_fwd_fp8(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), cos.data_ptr(), sin.data_ptr(), _DT[cos.dtype], cu.data_ptr(),
+            nseg, total, heads, hd, int(max_seqlen or 0), _DT[q.dtype], out.data_ptr(), ws.data_ptr() + off, ws_bytes,
+            _status_word(q.device).data_ptr(), torch.cuda.current_stream(q.device).cuda_stream,
+        )
+    _lib.check(rc, "frattn_fwd_fp8")
+    return out

@@ -191,6 +191,27 @@ int frattn_bwd(const void* q, const void* k, const void* v, const void* cos, con
                const void* out, const void* dout, const float* lse, void* dq, void* dk, void* dv,
                void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
 
+/* ---- FP8 (e4m3) q / k for long segments (the reference computes QK^T in
+ * the input type, fused_attn.py:394).
+ *
+ * frattn_fwd_fp8: the frattn_fwd operation with S = R(q) R(k)^T on the FP8
+ * tensor cores (tcgen05 kind::f8f6f4). A pre-pass rotates q and k in fp32 and
+ * rounds them to e4m3 with one scale per (token, head) row of q and one per head
+ * of k (scale = max |value| / 448); the scales are folded into the softmax
+ * exponent. P V stays in the input type. Same arguments as frattn_fwd; the
+ * workspace must hold frattn_workspace_bytes_fp8(T, nseg, H, D) bytes (the
+ * work list, the e4m3 copies of q and k and the scales) and be 256-byte
+ * aligned. D a multiple of 16 in [32, 128]. Accuracy: e4m3 keeps 3 mantissa bits, so scores carry about 2^-5
+ * relative error per product; on N(0, 1) inputs the output stays within
+ * max-abs 2e-2 / mean-abs 2e-3 of the fp32 path for long segments. Intended for
+ * long segments (all segments take the work-list path; windows gain nothing). */
+int frattn_workspace_bytes_fp8(int total_tokens, int num_segments, int num_heads, int head_dim,
+                               size_t* bytes);
+int frattn_fwd_fp8(const void* q, const void* k, const void* v, const void* cos, const void* sin,
+                   int cs_dtype, const int32_t* cu_seqlens, int nseg, int T, int H, int D,
+                   int max_seqlen, int in_dtype, void* out, void* workspace, size_t workspace_bytes,
+                   int32_t* status, void* stream);
+
 /* Allocation-free variant of frattn_fwd (no counterpart in the reference).
  *
  * For callers that cannot allocate device memory at the point of the call: a
