@@ -55,7 +55,7 @@ def parse():
     ap.add_argument("--no-encoder", action="store_true", help="skip the 32-layer encoder timing")
     ap.add_argument("--no-dp", action="store_true", help="skip the config-5 data-parallel sweep")
     ap.add_argument("--no-comparators", action="store_true", help="skip the same-box GPU comparators")
-    ap.add_argument("--profile", choices=["windowed", "full", "encoder"], default=None,
+    ap.add_argument("--profile", choices=["windowed", "full", "encoder", "qkv", "backward", "fp8"], default=None,
                     help="profiling case: windowed/full run --warmup + --steps eager calls of one layer kind "
                          "(for ncu); encoder prints a per-kernel breakdown of one 1344x1344 forward per arm")
     ap.add_argument("--images", type=int, default=1, help="896x896 images per call in --profile mode")
@@ -896,10 +896,32 @@ def run_profile_case(args):
     GRID = [(1, 64, 64)] * args.images
     dev = torch.device("cuda", 0)
     sets, T = make_inputs(torch, dev, seed=0)
-    t = sets[args.profile]
-    hint = 64 if args.profile == "windowed" else 4096
-    for _ in range(args.warmup + args.steps):
-        fused_rope_attention(t["q"], t["k"], t["v"], t["cos"], t["sin"], t["cu"], max_seqlen=hint)
+    n = args.warmup + args.steps
+    if args.profile == "qkv":  # one 1344x1344 layer's QKV projection with the RoPE epilogue
+        from fused_rope_attn_b200 import qkv_rope_projection
+        g = torch.Generator(device=dev).manual_seed(0)
+        x = torch.randn(9216, 1280, generator=g, device=dev).to(torch.bfloat16)
+        w = (torch.randn(3840, 1280, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        b = (torch.randn(3840, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        ang = torch.rand(9216, 40, generator=g, device=dev) * 50
+        for _ in range(n):
+            qkv_rope_projection(x, w, b, ang.cos(), ang.sin(), 16)
+        T = 9216
+    elif args.profile in ("backward", "fp8"):  # the config-2b full layer
+        from fused_rope_attn_b200 import fused_attn as FA
+        t = sets["full"]
+        if args.profile == "fp8":
+            for _ in range(n):
+                FA.fused_rope_attention_fp8(t["q"], t["k"], t["v"], t["cos"], t["sin"], t["cu"], max_seqlen=4096)
+        else:
+            out, lse = FA._fwd_lse(t["q"], t["k"], t["v"], t["cos"], t["sin"], t["cu"], 4096)
+            for _ in range(n):
+                FA._bwd(t["q"], t["k"], t["v"], t["cos"], t["sin"], t["cu"], out, lse, t["v"])
+    else:
+        t = sets[args.profile]
+        hint = 64 if args.profile == "windowed" else 4096
+        for _ in range(n):
+            fused_rope_attention(t["q"], t["k"], t["v"], t["cos"], t["sin"], t["cu"], max_seqlen=hint)
     torch.cuda.synchronize()
     assert last_status(dev) == 0
     print(json.dumps({"profile": args.profile, "images": args.images, "tokens": T, "calls": args.warmup + args.steps}))
