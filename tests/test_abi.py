@@ -117,3 +117,72 @@ def test_window_plan_sizes_match_host():
     bad = (ctypes.c_int32 * 3)(1, 15, 16)  # h not divisible by the merge size
     assert lib.frattn_window_plan_sizes(bad, 1, 112, 2, 14, ctypes.byref(u), ctypes.byref(w),
                                         ctypes.byref(ws)) == _lib.E_SHAPE
+
+
+def test_projection_and_rotated_entry_points_validate_arguments():
+    lib = _lib.load()
+
+    def qkv(**kw):
+        a = dict(x=16, xs=0, w=16, b=None, cos=16, sin=16, cs=_lib.F32, T=128, K=1280, H=16, D=80, dt=_lib.BF16,
+                 out=16)
+        a.update(kw)
+        return lib.frattn_qkv_rope(a["x"], a["xs"], a["w"], a["b"], a["cos"], a["sin"], a["cs"], a["T"], a["K"],
+                                   a["H"], a["D"], a["dt"], a["out"], None, None)
+    assert qkv(x=None) == _lib.E_NULL
+    assert qkv(D=72) == _lib.E_SHAPE            # head dims: multiples of 16
+    assert qkv(D=144) == _lib.E_SHAPE
+    assert qkv(K=1284) == _lib.E_ALIGN          # rows must be 16-byte multiples
+    assert qkv(xs=1000) == _lib.E_SHAPE         # stride below K
+    assert qkv(dt=_lib.F32) == _lib.E_DTYPE
+    assert qkv(cs=9) == _lib.E_DTYPE
+    assert qkv(w=24) == _lib.E_ALIGN
+    assert qkv(T=0) == 0                        # nothing to do, nothing launched
+
+    def rot(**kw):
+        a = dict(qs=0, T=128, H=2, D=80, dt=_lib.BF16, wsb=1 << 20)
+        a.update(kw)
+        return lib.frattn_fwd_rotated(16, 16, 16, a["qs"], 0, 0, 16, 1, a["T"], a["H"], a["D"], 0, a["dt"], 16, 16,
+                                      a["wsb"], None, None)
+    assert rot(qs=-1) == _lib.E_SHAPE
+    assert rot(D=74) == _lib.E_SHAPE
+    assert rot(dt=_lib.F32) == _lib.E_DTYPE
+    assert rot(wsb=8) == _lib.E_WORKSPACE
+
+
+def test_backward_and_fp8_entry_points_validate_arguments():
+    import ctypes
+    lib = _lib.load()
+    assert _lib.workspace_bytes_bwd(4096, 16, 80) >= 4096 * 16 * 80 * (2 + 2 + 4)
+    assert _lib.workspace_bytes_fp8(4096, 1, 16, 80) >= _lib.workspace_bytes(4096, 1) + 2 * 4096 * 16 * 80
+
+    def bwd(**kw):
+        a = dict(q=16, T=128, H=2, D=80, dt=_lib.BF16, cs=_lib.F32, lse=16, wsb=1 << 30)
+        a.update(kw)
+        return lib.frattn_bwd(a["q"], 16, 16, 16, 16, a["cs"], 16, 1, a["T"], a["H"], a["D"], a["dt"], 16, 16,
+                              a["lse"], 16, 16, 16, 16, a["wsb"], None, None)
+    assert bwd(q=None) == _lib.E_NULL
+    assert bwd(D=96) == _lib.E_SHAPE            # backward head dims: 32, 48, 64, 80
+    assert bwd(dt=_lib.F32) == _lib.E_DTYPE
+    assert bwd(cs=5) == _lib.E_DTYPE
+    assert bwd(lse=18) == _lib.E_ALIGN
+    assert bwd(wsb=16) == _lib.E_WORKSPACE
+
+    def fp8(**kw):
+        a = dict(D=80, ws=256, wsb=1 << 30, dt=_lib.BF16)
+        a.update(kw)
+        return lib.frattn_fwd_fp8(16, 16, 16, 16, 16, _lib.F32, 16, 1, 128, 2, a["D"], 0, a["dt"], 16, a["ws"],
+                                  a["wsb"], None, None)
+    assert fp8(D=72) == _lib.E_SHAPE
+    assert fp8(dt=_lib.F32) == _lib.E_DTYPE
+    assert fp8(ws=272) == _lib.E_ALIGN          # workspace 256-byte aligned
+    assert fp8(wsb=1024) == _lib.E_WORKSPACE
+    out = ctypes.c_size_t(0)
+    assert lib.frattn_workspace_bytes_fp8(10, 0, 1, 80, ctypes.byref(out)) == _lib.E_SHAPE
+
+
+def test_training_wrapper_rejects_unsupported_head_dim_on_cpu():
+    import torch
+    from fused_rope_attn_b200 import fused_rope_attention_train
+    q = torch.zeros(4, 1, 80, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        fused_rope_attention_train(q, q, q, torch.zeros(4, 40), torch.zeros(4, 40), torch.tensor([0, 4]))
