@@ -12,7 +12,8 @@
 //   bwd_prep      one thread per (token, head): rotated q and k into the
 //                 workspace (fp32 math, one rounding, as the forward), the row
 //                 term rowsum(dO o O), and a zeroed fp32 dq accumulator row
-//   bwd_main      one CTA per (128-key chunk of the packed sequence, head):
+//   bwd_main      one CTA per (128-key chunk of the packed sequence, head),
+//                 head dims that are multiples of 16 up to 128:
 //                 the chunk's keys attend to the queries of their own segments,
 //                 so the CTA walks the q tiles of the segments that overlap the
 //                 chunk (windows: one tile; a long segment: all of its tiles).
@@ -53,18 +54,21 @@ struct BwdParams {
 
 template <int D>
 struct BwdCfg {
-  static_assert(D % 16 == 0 && D >= 32 && D <= 80, "backward: D a multiple of 16 in [32, 80]");
+  static_assert(D % 16 == 0 && D >= 32 && D <= 128, "backward: D a multiple of 16 in [32, 128]");
   static constexpr int KB = D / 16;
   static constexpr int TILE = kTileM * D * 2;       // one 128 x D tile
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + TILE;
-  static constexpr int OFF_Q = OFF_V + TILE;        // [2] stages
-  static constexpr int OFF_DO = OFF_Q + 2 * TILE;   // [2]
-  static constexpr int OFF_DS = OFF_DO + 2 * TILE;  // dS^T as an MN-major [128 q x 128 keys] operand
   static constexpr int DS_BYTES = 128 * 128 * 2;
+  // Q / dO stages: two when they fit in 227 KB, else one (D = 128)
+  static constexpr int QS = (2 + 4) * TILE + DS_BYTES + 2048 + 256 + 1024 <= 232448 ? 2 : 1;
+  static constexpr int OFF_Q = OFF_V + TILE;         // [QS] stages
+  static constexpr int OFF_DO = OFF_Q + QS * TILE;   // [QS]
+  static constexpr int OFF_DS = OFF_DO + QS * TILE;  // dS^T as an MN-major [128 q x 128 keys] operand
   static constexpr int OFF_VEC = OFF_DS + DS_BYTES; // lse2, delta of the q tile: [2][2][128] fp32
   static constexpr int OFF_BAR = OFF_VEC + 2 * 2 * 128 * 4;
   static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static_assert(SMEM <= 232448, "shared memory");
   // TMEM columns (every accumulator starts on a 128-column boundary): S^T / P^T,
   // then the dQ tile once dV has read P^T; dP^T / dS^T; dV; dK
   static constexpr uint32_t T_S = 0, T_DQ = 0, T_DP = 128, T_DV = 256, T_DK = 384;
@@ -274,8 +278,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_main(const __grid_constant
       }
       int i = 0;
       for (; i < nq; ++i) {
-        const int s = i & 1;
-        if (!bwd_wait(bar(EMPTY + s), ((i >> 1) & 1) ^ 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x61))
+        const int s = i % C::QS;
+        if (!bwd_wait(bar(EMPTY + s), ((i / C::QS) & 1) ^ 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x61))
           break;
         const int q0 = q_tile(i);
         mbar_arrive_expect_tx(bar(FULL + s), 2 * C::TILE);
@@ -287,7 +291,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_main(const __grid_constant
       }
       // copies in flight land before the CTA exits
       bwd_drain(bar(KV_FULL), 0, p.wait_limit_ns);
-      for (int j = max(0, i - 2); j < i; ++j) bwd_drain(bar(FULL + (j & 1)), (j >> 1) & 1, p.wait_limit_ns);
+      for (int j = max(0, i - C::QS); j < i; ++j) bwd_drain(bar(FULL + j % C::QS), (j / C::QS) & 1, p.wait_limit_ns);
     }
   } else if (warp == 1) {
     if (lane == 0 && nq > 0) {
@@ -299,8 +303,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_main(const __grid_constant
       const uint64_t k_mn = make_sdesc(kaddr, kBlkBytes, 256, SW32);  // K as an MN-major B
       const uint64_t ds_mn = make_sdesc(sbase + C::OFF_DS, kBlkBytes, 256, SW32);
       for (int i = 0; i < nq && ok; ++i) {
-        const int s = i & 1;
-        ok = bwd_wait(bar(FULL + s), (i >> 1) & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x63);
+        const int s = i % C::QS;
+        ok = bwd_wait(bar(FULL + s), (i / C::QS) & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x63);
         BT(0, i);
         if (!ok) break;
         tc_fence_after();
@@ -689,7 +693,7 @@ extern "C" int frattn_bwd(const void* q, const void* k, const void* v, const voi
   if (!q || !k || !v || !cos || !sin || !cu_seqlens || !out || !dout || !lse || !dq || !dk || !dv || !workspace)
     return FRATTN_E_NULL;
   if (T < 0 || H <= 0 || nseg < 1) return FRATTN_E_SHAPE;
-  if (D != 32 && D != 48 && D != 64 && D != 80) return FRATTN_E_SHAPE;
+  if (D % 16 != 0 || D < 32 || D > 128) return FRATTN_E_SHAPE;
   if (static_cast<long long>(T) * H * D >= (1ll << 31)) return FRATTN_E_SHAPE;
   if (in_dtype != FRATTN_BF16 && in_dtype != FRATTN_F16) return FRATTN_E_DTYPE;
   if (cs_dtype != FRATTN_F32 && cs_dtype != FRATTN_BF16 && cs_dtype != FRATTN_F16) return FRATTN_E_DTYPE;
@@ -708,6 +712,9 @@ extern "C" int frattn_bwd(const void* q, const void* k, const void* v, const voi
     case 48: return bwd_in<48>(in_dtype, cs_dtype, q, k, v, cos, sin, cu_seqlens, nseg, T, H, out, dout, lse, dq, dk, dv, ws, status, st);
     case 64: return bwd_in<64>(in_dtype, cs_dtype, q, k, v, cos, sin, cu_seqlens, nseg, T, H, out, dout, lse, dq, dk, dv, ws, status, st);
     case 80: return bwd_in<80>(in_dtype, cs_dtype, q, k, v, cos, sin, cu_seqlens, nseg, T, H, out, dout, lse, dq, dk, dv, ws, status, st);
+    case 96: return bwd_in<96>(in_dtype, cs_dtype, q, k, v, cos, sin, cu_seqlens, nseg, T, H, out, dout, lse, dq, dk, dv, ws, status, st);
+    case 112: return bwd_in<112>(in_dtype, cs_dtype, q, k, v, cos, sin, cu_seqlens, nseg, T, H, out, dout, lse, dq, dk, dv, ws, status, st);
+    case 128: return bwd_in<128>(in_dtype, cs_dtype, q, k, v, cos, sin, cu_seqlens, nseg, T, H, out, dout, lse, dq, dk, dv, ws, status, st);
     default: return FRATTN_E_SHAPE;
   }
 }

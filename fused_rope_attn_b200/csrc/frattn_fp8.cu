@@ -13,8 +13,9 @@
 //   fp8_quantize one thread per (token, head): R(q) / s_q(t,h) and R(k) / s_k(h)
 //                rounded to e4m3 (saturating), rows padded with zeros to a
 //                multiple of 16 bytes; s = amax / 448 (the e4m3 maximum).
-//                Rows are read and written as 16-byte vectors (head dims that
-//                are multiples of 16).
+//                Eight lanes per row (one 8-element chunk of each half each,
+//                16-byte loads, shuffle-reduced row maxima; head dims that are
+//                multiples of 16).
 // then the persistent attention kernel in its kRopeFp8 mode (work list as for
 // frattn_fwd, no rotation, no K pre-rotation pass).
 #include <cuda_fp8.h>
@@ -32,48 +33,39 @@ namespace {
 
 constexpr float kE4M3Max = 448.f;
 
-// Rotated row (fp32) of a [T, H, D] tensor: 8-element chunks of both halves
-// loaded as 16-byte vectors, one rounding-free fp32 rotation (as the forward).
+// Eight lanes per (token, head) row: lane c < D/16 owns the 8-element chunk c of
+// each rotate-half half (16-byte loads), rotates it in fp32 and the row's
+// max |value| is reduced over the eight lanes with shuffles.
 template <int D, typename TI, typename TC>
-__device__ __forceinline__ void rotated_row(const TI* __restrict__ x, const TC* __restrict__ cs,
-                                            const TC* __restrict__ sn, float (&y)[D]) {
+__device__ __forceinline__ void rotated_chunk(const TI* __restrict__ x, const TC* __restrict__ cs,
+                                              const TC* __restrict__ sn, int c, float (&y0)[8], float (&y1)[8]) {
+  float c8[8], s8[8], x0[8], x1[8];
+  load8<TC>(cs + 8 * c, c8);
+  load8<TC>(sn + 8 * c, s8);
+  unpack8<TI>(__ldg(reinterpret_cast<const uint4*>(x + 8 * c)), x0);
+  unpack8<TI>(__ldg(reinterpret_cast<const uint4*>(x + D / 2 + 8 * c)), x1);
 #pragma unroll
-  for (int c = 0; c < D / 16; ++c) {
-    float c8[8], s8[8], x0[8], x1[8];
-    load8<TC>(cs + 8 * c, c8);
-    load8<TC>(sn + 8 * c, s8);
-    unpack8<TI>(__ldg(reinterpret_cast<const uint4*>(x + 8 * c)), x0);
-    unpack8<TI>(__ldg(reinterpret_cast<const uint4*>(x + D / 2 + 8 * c)), x1);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      y[8 * c + e] = x0[e] * c8[e] - x1[e] * s8[e];
-      y[D / 2 + 8 * c + e] = x0[e] * s8[e] + x1[e] * c8[e];
-    }
+  for (int e = 0; e < 8; ++e) {
+    y0[e] = x0[e] * c8[e] - x1[e] * s8[e];
+    y1[e] = x0[e] * s8[e] + x1[e] * c8[e];
   }
 }
 
-// e4m3 row of D values (times inv) padded with zeros to D16 bytes, 16-byte stores.
-template <int D>
-__device__ __forceinline__ void store_e4m3(uint8_t* __restrict__ dst, const float (&y)[D], float inv) {
-  constexpr int D16 = (D + 15) / 16 * 16;
+__device__ __forceinline__ float max8_lanes(float m) {
 #pragma unroll
-  for (int c = 0; c < D16 / 16; ++c) {
-    uint32_t w[4];
+  for (int o = 1; o < 8; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  return m;
+}
+
+__device__ __forceinline__ uint2 pack8_e4m3(const float (&y)[8], float inv) {
+  uint32_t w[2];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      uint32_t word = 0;
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        const int i0 = 16 * c + 4 * u + e;
-        const float a = i0 < D ? y[i0 < D ? i0 : 0] * inv : 0.f;
-        const float b = i0 + 1 < D ? y[i0 + 1 < D ? i0 + 1 : 0] * inv : 0.f;
-        const uint32_t pr = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
-        word |= pr << (8 * e);
-      }
-      w[u] = word;
-    }
-    *reinterpret_cast<uint4*>(dst + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
+  for (int u = 0; u < 2; ++u) {
+    const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(y[4 * u] * inv, y[4 * u + 1] * inv), __NV_SATFINITE, __NV_E4M3);
+    const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(y[4 * u + 2] * inv, y[4 * u + 3] * inv), __NV_SATFINITE, __NV_E4M3);
+    w[u] = lo | (hi << 16);
   }
+  return make_uint2(w[0], w[1]);
 }
 
 template <int D, typename TI, typename TC>
@@ -85,17 +77,22 @@ __global__ void __launch_bounds__(256) fp8_k_amax(const TI* __restrict__ k, cons
   __shared__ unsigned int smax[256];
   smax[threadIdx.x] = 0u;
   __syncthreads();
-  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long g = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long i = g >> 3;  // row (token, head)
+  const int c = static_cast<int>(g & 7);
   const bool in = i < static_cast<long long>(T) * H;
   const int h = static_cast<int>(i % H);
-  if (in) {
+  float m = 0.f;
+  if (in && c < D / 16) {
     const int t = static_cast<int>(i / H);
-    float y[D];
-    rotated_row<D, TI, TC>(k + static_cast<size_t>(i) * D, cos + static_cast<size_t>(t) * (D / 2),
-                           sin + static_cast<size_t>(t) * (D / 2), y);
-    float m = 0.f;
+    float y0[8], y1[8];
+    rotated_chunk<D, TI, TC>(k + static_cast<size_t>(i) * D, cos + static_cast<size_t>(t) * (D / 2),
+                             sin + static_cast<size_t>(t) * (D / 2), c, y0, y1);
 #pragma unroll
-    for (int e = 0; e < D; ++e) m = fmaxf(m, fabsf(y[e]));
+    for (int e = 0; e < 8; ++e) m = fmaxf(m, fmaxf(fabsf(y0[e]), fabsf(y1[e])));
+  }
+  m = max8_lanes(m);
+  if (in && c == 0) {
     if (H <= 256)
       atomicMax(smax + h, __float_as_uint(m));
     else
@@ -112,25 +109,38 @@ __global__ void __launch_bounds__(256) fp8_quantize(const TI* __restrict__ q, co
                                                     int T, int H, const unsigned int* __restrict__ kamax,
                                                     uint8_t* __restrict__ q8, uint8_t* __restrict__ k8,
                                                     float* __restrict__ qscale, float* __restrict__ kscale) {
-  constexpr int D16 = (D + 15) / 16 * 16;
-  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= static_cast<long long>(T) * H) return;
-  const int t = static_cast<int>(i / H), h = static_cast<int>(i % H);
+  constexpr int D16 = (D + 15) / 16 * 16;  // == D (head dims here are multiples of 16)
+  static_assert(D16 == D, "multiples of 16");
+  const long long g = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long i = g >> 3;
+  const int c = static_cast<int>(g & 7);
+  const bool in = i < static_cast<long long>(T) * H;
+  const bool act = in && c < D / 16;
+  const int t = in ? static_cast<int>(i / H) : 0, h = static_cast<int>(i % H);
   const TC* cs = cos + static_cast<size_t>(t) * (D / 2);
   const TC* sn = sin + static_cast<size_t>(t) * (D / 2);
-  float y[D];
-  rotated_row<D, TI, TC>(q + static_cast<size_t>(i) * D, cs, sn, y);
-  float mq = 0.f;
+  float y0[8], y1[8];
+  float m = 0.f;
+  if (act) {
+    rotated_chunk<D, TI, TC>(q + static_cast<size_t>(i) * D, cs, sn, c, y0, y1);
 #pragma unroll
-  for (int e = 0; e < D; ++e) mq = fmaxf(mq, fabsf(y[e]));
-  const float sq = mq > 0.f ? mq / kE4M3Max : 1.f;
-  store_e4m3<D>(q8 + static_cast<size_t>(i) * D16, y, 1.f / sq);
-  qscale[i] = sq;
-  rotated_row<D, TI, TC>(k + static_cast<size_t>(i) * D, cs, sn, y);
-  const float mk = __uint_as_float(__ldg(kamax + h));
-  const float sk = mk > 0.f ? mk / kE4M3Max : 1.f;
-  store_e4m3<D>(k8 + static_cast<size_t>(i) * D16, y, 1.f / sk);
-  if (t == 0) kscale[h] = sk;
+    for (int e = 0; e < 8; ++e) m = fmaxf(m, fmaxf(fabsf(y0[e]), fabsf(y1[e])));
+  }
+  m = max8_lanes(m);
+  const float sq = m > 0.f ? m / kE4M3Max : 1.f;
+  if (act) {
+    uint8_t* row = q8 + static_cast<size_t>(i) * D;
+    *reinterpret_cast<uint2*>(row + 8 * c) = pack8_e4m3(y0, 1.f / sq);
+    *reinterpret_cast<uint2*>(row + D / 2 + 8 * c) = pack8_e4m3(y1, 1.f / sq);
+    if (c == 0) qscale[i] = sq;
+    const float mk = __uint_as_float(__ldg(kamax + h));
+    const float sk = mk > 0.f ? mk / kE4M3Max : 1.f;
+    rotated_chunk<D, TI, TC>(k + static_cast<size_t>(i) * D, cs, sn, c, y0, y1);
+    uint8_t* krow = k8 + static_cast<size_t>(i) * D;
+    *reinterpret_cast<uint2*>(krow + 8 * c) = pack8_e4m3(y0, 1.f / sk);
+    *reinterpret_cast<uint2*>(krow + D / 2 + 8 * c) = pack8_e4m3(y1, 1.f / sk);
+    if (t == 0 && c == 0) kscale[h] = sk;
+  }
 }
 
 struct Fp8Layout {
@@ -157,7 +167,7 @@ template <int D, typename TI, typename TC>
 int quantize_d(const void* q, const void* k, const void* cos, const void* sin, int T, int H, uint8_t* ws,
                const Fp8Layout& L, cudaStream_t st) {
   const long long rows = static_cast<long long>(T) * H;
-  const int blocks = static_cast<int>((rows + 255) / 256);
+  const int blocks = static_cast<int>((rows * 8 + 255) / 256);  // eight lanes per row
   unsigned int* kamax = reinterpret_cast<unsigned int*>(ws + L.kamax);
   if (cudaMemsetAsync(kamax, 0, static_cast<size_t>(H) * 4, st) != cudaSuccess) return FRATTN_E_CUDA;
   fp8_k_amax<D, TI, TC><<<blocks, 256, 0, st>>>(static_cast<const TI*>(k), static_cast<const TC*>(cos),

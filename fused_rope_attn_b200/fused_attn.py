@@ -508,7 +508,7 @@ def fused_attention_rotated(
 
 
 # --------------------------------------------------------------------------- backward
-BACKWARD_HEAD_DIMS = (32, 48, 64, 80)
+BACKWARD_HEAD_DIMS = (32, 48, 64, 80, 96, 112, 128)
 
 
 def _fwd_lse(q, k, v, cos, sin, cu, max_seqlen):

@@ -179,7 +179,7 @@ int frattn_fwd_rotated(const void* q, const void* k, const void* v, long long q_
  * P = softmax(R(q) R(k)^T / sqrt(D)) per segment and head, R^T the inverse
  * rotation. cos/sin are constants (no gradient). Rows outside every segment
  * get zero gradients. All tensors contiguous [T, H, D] (cos/sin [T, D/2]);
- * D in {32, 48, 64, 80}; workspace >= frattn_workspace_bytes_bwd(T, H, D)
+ * D a multiple of 16 in [32, 128]; workspace >= frattn_workspace_bytes_bwd(T, H, D)
  * bytes (rotated q and k, the row terms and an fp32 dq accumulator). */
 int frattn_fwd_lse(const void* q, const void* k, const void* v, const void* cos, const void* sin,
                    int cs_dtype, const int32_t* cu_seqlens, int nseg, int T, int H, int D,

@@ -161,7 +161,8 @@ def test_backward_and_fp8_entry_points_validate_arguments():
         return lib.frattn_bwd(a["q"], 16, 16, 16, 16, a["cs"], 16, 1, a["T"], a["H"], a["D"], a["dt"], 16, 16,
                               a["lse"], 16, 16, 16, 16, a["wsb"], None, None)
     assert bwd(q=None) == _lib.E_NULL
-    assert bwd(D=96) == _lib.E_SHAPE            # backward head dims: 32, 48, 64, 80
+    assert bwd(D=72) == _lib.E_SHAPE            # backward head dims: multiples of 16
+    assert bwd(D=144) == _lib.E_SHAPE
     assert bwd(dt=_lib.F32) == _lib.E_DTYPE
     assert bwd(cs=5) == _lib.E_DTYPE
     assert bwd(lse=18) == _lib.E_ALIGN

@@ -90,6 +90,9 @@ def run_case(cu_list, H, D, dtype=torch.bfloat16, cs_dtype=torch.float32, T=None
     ([0, 1, 2, 130, 258, 259], 1, 64, None),           # one-token segments
     ([0, 0, 200, 200, 330], 2, 48, None),              # empty segments
     ([0, 256, 512], 2, 32, None),
+    ([0, 300, 700], 2, 96, None),
+    ([0, 64, 128, 200, 520], 2, 112, 128),
+    ([0, 400, 660], 2, 128, None),                     # one Q/dO stage (shared memory)
 ])
 def test_backward_matches_fp32_autograd(cu, H, D, hint):
     run_case(cu, H, D, hint=hint)
@@ -123,6 +126,6 @@ def test_forward_lse_and_output():
 
 
 def test_backward_rejects_unsupported_head_dim():
-    q, k, v, cos, sin, cu = cu_case([0, 64], H=1, D=96)
+    q, k, v, cos, sin, cu = cu_case([0, 64], H=1, D=72)
     with pytest.raises(ValueError):
         fused_rope_attention_train(q.to(DEV), k.to(DEV), v.to(DEV), cos.to(DEV), sin.to(DEV), cu.to(DEV))
