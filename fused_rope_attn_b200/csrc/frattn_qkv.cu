@@ -32,6 +32,12 @@ namespace frattn {
 
 unsigned long long frattn_wait_limit_ns();  // frattn.cu
 
+// Kernel choice for frattn_qkv_rope: CTA pairs (default) or single CTAs.
+static int g_qkv_pairs = 1;
+static bool qkv_use_pairs() { return g_qkv_pairs != 0; }
+
+constexpr int kQkvThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+
 struct QkvParams {
   CUtensorMap tma_x, tma_w;
   const void* bias;  // [N] or nullptr
@@ -96,8 +102,66 @@ __device__ __forceinline__ void load8_in(const TI* src, float (&v)[8]) {
 
 }  // namespace
 
+// Epilogue of one tile for the thread of accumulator row `row`: whole heads of
+// the N tile [n0, n0 + HPT D) from TMEM columns acc.. (bias, rounding to the
+// input type, rotation of q / k heads, 16-byte stores).
+template <int D, int HPT, typename TI, typename TC>
+__device__ __forceinline__ void qkv_tile_epilogue(const QkvParams& p, uint32_t acc, int row, int n0) {
+  const TI* bias = static_cast<const TI*>(p.bias);
+  TI* out = static_cast<TI*>(p.out);
+#pragma unroll 1
+  for (int hh = 0; hh < HPT; ++hh) {
+    const int n = n0 + hh * D;
+    if (n >= p.N) break;
+    uint32_t v[D];
+#pragma unroll
+    for (int c = 0; c < D / 16; ++c) {
+      uint32_t (&chunk)[16] = *reinterpret_cast<uint32_t(*)[16]>(&v[16 * c]);
+      tmem_ld16(acc + hh * D + 16 * c, chunk);
+    }
+    tmem_ld_wait();
+    if (row >= p.T) continue;
+    float x[D];
+#pragma unroll
+    for (int c = 0; c < D / 8; ++c) {
+      float b[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (bias) load8_in<TI>(bias + n + 8 * c, b);
+#pragma unroll
+      for (int e = 0; e < 8; ++e)  // the value a plain projection stores
+        x[8 * c + e] = to_f32<TI>(from_f32<TI>(__uint_as_float(v[8 * c + e]) + b[e]));
+    }
+    const int part = (n / D) / p.H;  // 0 q, 1 k, 2 v
+    if (part < 2) {
+      const TC* cr = static_cast<const TC*>(p.cos) + static_cast<size_t>(row) * (D / 2);
+      const TC* sr = static_cast<const TC*>(p.sin) + static_cast<size_t>(row) * (D / 2);
+#pragma unroll
+      for (int c = 0; c < D / 16; ++c) {
+        float cs[8], sn[8];
+        load8<TC>(cr + 8 * c, cs);
+        load8<TC>(sr + 8 * c, sn);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float x0 = x[8 * c + e], x1 = x[8 * c + e + D / 2];
+          x[8 * c + e] = x0 * cs[e] - x1 * sn[e];
+          x[8 * c + e + D / 2] = x0 * sn[e] + x1 * cs[e];
+        }
+      }
+    }
+    TI* dst = out + static_cast<size_t>(row) * p.N + n;
+#pragma unroll
+    for (int c = 0; c < D / 8; ++c) {
+      uint4 w;
+      w.x = pack2<TI>(x[8 * c + 0], x[8 * c + 1]);
+      w.y = pack2<TI>(x[8 * c + 2], x[8 * c + 3]);
+      w.z = pack2<TI>(x[8 * c + 4], x[8 * c + 5]);
+      w.w = pack2<TI>(x[8 * c + 6], x[8 * c + 7]);
+      *reinterpret_cast<uint4*>(dst + 8 * c) = w;
+    }
+  }
+}
+
 template <int D, typename TI, typename TC>
-__global__ void __launch_bounds__(192, 1) qkv_rope_gemm_kernel(const __grid_constant__ QkvParams p) {
+__global__ void __launch_bounds__(kQkvThreads, 1) qkv_rope_gemm_kernel(const __grid_constant__ QkvParams p) {
   using C = QkvCfg<D>;
   constexpr int ST = C::ST;
   constexpr bool kBF16 = std::is_same<TI, __nv_bfloat16>::value;
@@ -199,8 +263,6 @@ __global__ void __launch_bounds__(192, 1) qkv_rope_gemm_kernel(const __grid_cons
     const int ew = warp & 3;  // TMEM lane quarter this warp may access
     const int r = ew * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(ew * 32) << 16);
-    const TI* bias = static_cast<const TI*>(p.bias);
-    TI* out = static_cast<TI*>(p.out);
     uint32_t lt = 0;
     for (int t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++lt) {
       const int buf = lt & 1;
@@ -208,56 +270,7 @@ __global__ void __launch_bounds__(192, 1) qkv_rope_gemm_kernel(const __grid_cons
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       const int m0 = (t / p.n_tiles_n) * C::BM, n0 = (t % p.n_tiles_n) * C::BN;
-      const int row = m0 + r;
-#pragma unroll 1
-      for (int hh = 0; hh < C::HPT; ++hh) {
-        const int n = n0 + hh * D;
-        if (n >= p.N) break;
-        uint32_t v[D];
-#pragma unroll
-        for (int c = 0; c < D / 16; ++c) {
-          uint32_t (&chunk)[16] = *reinterpret_cast<uint32_t(*)[16]>(&v[16 * c]);
-          tmem_ld16(lane_base + buf * 256u + hh * D + 16 * c, chunk);
-        }
-        tmem_ld_wait();
-        if (row >= p.T) continue;
-        float x[D];
-#pragma unroll
-        for (int c = 0; c < D / 8; ++c) {
-          float b[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-          if (bias) load8_in<TI>(bias + n + 8 * c, b);
-#pragma unroll
-          for (int e = 0; e < 8; ++e)  // the value a plain projection stores
-            x[8 * c + e] = to_f32<TI>(from_f32<TI>(__uint_as_float(v[8 * c + e]) + b[e]));
-        }
-        const int part = (n / D) / p.H;  // 0 q, 1 k, 2 v
-        if (part < 2) {
-          const TC* cr = static_cast<const TC*>(p.cos) + static_cast<size_t>(row) * (D / 2);
-          const TC* sr = static_cast<const TC*>(p.sin) + static_cast<size_t>(row) * (D / 2);
-#pragma unroll
-          for (int c = 0; c < D / 16; ++c) {
-            float cs[8], sn[8];
-            load8<TC>(cr + 8 * c, cs);
-            load8<TC>(sr + 8 * c, sn);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float x0 = x[8 * c + e], x1 = x[8 * c + e + D / 2];
-              x[8 * c + e] = x0 * cs[e] - x1 * sn[e];
-              x[8 * c + e + D / 2] = x0 * sn[e] + x1 * cs[e];
-            }
-          }
-        }
-        TI* dst = out + static_cast<size_t>(row) * p.N + n;
-#pragma unroll
-        for (int c = 0; c < D / 8; ++c) {
-          uint4 w;
-          w.x = pack2<TI>(x[8 * c + 0], x[8 * c + 1]);
-          w.y = pack2<TI>(x[8 * c + 2], x[8 * c + 3]);
-          w.z = pack2<TI>(x[8 * c + 4], x[8 * c + 5]);
-          w.w = pack2<TI>(x[8 * c + 6], x[8 * c + 7]);
-          *reinterpret_cast<uint4*>(dst + 8 * c) = w;
-        }
-      }
+      qkv_tile_epilogue<D, C::HPT, TI, TC>(p, lane_base + buf * 256u, m0 + r, n0);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(ACC_EMPTY + buf));
@@ -268,6 +281,162 @@ __global__ void __launch_bounds__(192, 1) qkv_rope_gemm_kernel(const __grid_cons
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ CTA pairs
+// The same GEMM on CTA pairs (cluster of 2, tcgen05 cta_group::2): one MMA of
+// M = 256 spans both CTAs. Each CTA loads its own 128 rows of x and half of the
+// N tile's W rows (BN/2), so a pair moves 2 x (16 + BN/16) KB per 64-wide K step
+// for twice the FLOPs of one CTA: a third less operand traffic per FLOP than the
+// single-CTA kernel. Each CTA's TMEM holds its 128 accumulator rows x BN columns
+// (two buffers); both CTAs run the epilogue of their rows. The leader CTA (rank
+// 0) owns the stage barriers that count both CTAs' TMA bytes and issues the
+// MMAs; its commits arrive on both CTAs' barriers (multicast commit); the peer's
+// epilogue warps arrive on the leader's accumulator-free barrier.
+template <int D>
+struct QkvPairCfg {
+  static constexpr int HPT = 256 / D;
+  static constexpr int BN = HPT * D;  // N tile of the pair
+  static constexpr int BNH = BN / 2;  // W rows loaded by each CTA
+  static constexpr int BK = 64;
+  static constexpr int A_BYTES = 128 * BK * 2;
+  static constexpr int B_BYTES = BNH * BK * 2;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int ST_FIT = (227 * 1024 - 2048) / STAGE;
+  static constexpr int ST = ST_FIT > 6 ? 6 : ST_FIT;
+  static constexpr int OFF_BAR = ST * STAGE;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static_assert(BN % 16 == 0 && BN <= 256 && BNH % 8 == 0, "UMMA N / swizzle atoms");
+  static_assert(B_BYTES % 1024 == 0, "128-B swizzle atoms");
+};
+
+template <int D, typename TI, typename TC>
+__global__ void __launch_bounds__(kQkvThreads, 1) qkv_rope_gemm_pair_kernel(const __grid_constant__ QkvParams p) {
+  using C = QkvPairCfg<D>;
+  constexpr int ST = C::ST;
+  constexpr bool kBF16 = std::is_same<TI, __nv_bfloat16>::value;
+  constexpr uint32_t IDESC = make_idesc_f16(kBF16, 256, C::BN, false);
+  constexpr uint32_t SW128 = 2;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  auto bar = [&](int i) { return smem_u32(bars + i); };
+  const int FULL = 0, EMPTY = ST, ACC_FULL = 2 * ST, ACC_EMPTY = 2 * ST + 2, DRAIN = 2 * ST + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ST; ++i) {
+      mbar_init(bar(FULL + i), 1);   // the leader's producer arrives; both CTAs' bytes complete it
+      mbar_init(bar(EMPTY + i), 1);  // multicast commit of the leader's MMAs
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(ACC_FULL + i), 1);
+      mbar_init(bar(ACC_EMPTY + i), 8);  // 4 epilogue warps of each CTA (used in the leader)
+    }
+    mbar_init(bar(DRAIN), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&p.tma_x);
+    tma_prefetch_desc(&p.tma_w);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int nk = (p.K + C::BK - 1) / C::BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer (both CTAs)
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = pair; t < p.n_tiles && ok; t += npairs) {
+        const int m0 = (t / p.n_tiles_n) * 256 + 128 * static_cast<int>(rank);
+        const int n0 = (t % p.n_tiles_n) * C::BN + C::BNH * static_cast<int>(rank);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % ST;
+          if (!qkv_wait(bar(EMPTY + s), ((it / ST) & 1) ^ 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x35)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(bar(FULL + s), 2 * C::STAGE);
+          const uint32_t full0 = mapa_shared(bar(FULL + s), 0);  // the leader's stage barrier
+          uint8_t* a = smem + s * C::STAGE;
+          tma_load_2d_pair(smem_u32(a), &p.tma_x, full0, kb * C::BK, m0);
+          tma_load_2d_pair(smem_u32(a + C::A_BYTES), &p.tma_w, full0, kb * C::BK, n0);
+        }
+      }
+      if (leader) {  // copies of both CTAs still in flight land before the pair exits
+        const uint32_t first = it > static_cast<uint32_t>(ST) ? it - ST : 0;
+        for (uint32_t i = first; i < it; ++i) qkv_drain(bar(FULL + i % ST), (i / ST) & 1, p.wait_limit_ns);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------------------------------------------------- MMA issuer (leader)
+      uint32_t it = 0, lt = 0;
+      bool ok = true;
+      for (int t = pair; t < p.n_tiles && ok; t += npairs, ++lt) {
+        const int buf = lt & 1;
+        if (!qkv_wait(bar(ACC_EMPTY + buf), ((lt >> 1) & 1) ^ 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x36))
+          break;
+        tc_fence_after();
+        const uint32_t d = tmem + buf * 256u;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % ST;
+          if (!qkv_wait(bar(FULL + s), (it / ST) & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x37)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(smem + s * C::STAGE);
+          const uint64_t ad = make_sdesc(a, 16, 1024, SW128);
+          const uint64_t bd = make_sdesc(a + C::A_BYTES, 16, 1024, SW128);
+#pragma unroll
+          for (int kk = 0; kk < C::BK / 16; ++kk)
+            umma_ss_pair(d, ad + 2 * kk, bd + 2 * kk, IDESC, (kb | kk) != 0);
+          umma_commit_pair_mc(bar(EMPTY + s), 0x3);
+        }
+        if (ok) umma_commit_pair_mc(bar(ACC_FULL + buf), 0x3);
+      }
+      umma_commit_pair_mc(bar(DRAIN), 0x1);
+      qkv_drain(bar(DRAIN), 0, p.wait_limit_ns);
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue (both CTAs)
+    const int ew = warp & 3;
+    const int r = ew * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(ew * 32) << 16);
+    const uint32_t acc_empty0 = mapa_shared(bar(ACC_EMPTY), 0);
+    uint32_t lt = 0;
+    for (int t = pair; t < p.n_tiles; t += npairs, ++lt) {
+      const int buf = lt & 1;
+      const bool ok = qkv_wait(bar(ACC_FULL + buf), (lt >> 1) & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x38);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const int m0 = (t / p.n_tiles_n) * 256 + 128 * static_cast<int>(rank), n0 = (t % p.n_tiles_n) * C::BN;
+      qkv_tile_epilogue<D, C::HPT, TI, TC>(p, lane_base + buf * 256u, m0 + r, n0);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8u * buf);
+    }
+  }
+  tc_fence_before();
+  cluster_sync_all();  // no CTA leaves while its pair may still signal it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 
@@ -300,9 +469,48 @@ static int make_kmajor_map(CUtensorMap* m, const void* base, int rows, int K, lo
   return r == CUDA_SUCCESS ? 0 : FRATTN_E_TMAP;
 }
 
+// CTA-pair launch (cluster of 2).
+template <int D, typename TI, typename TC>
+static int launch_qkv_pair(QkvParams& p, const void* x, long long ldx, const void* w, bool bf16,
+                           cudaStream_t st) {
+  using C = QkvPairCfg<D>;
+  if (make_kmajor_map(&p.tma_x, x, p.T, p.K, ldx, 128, bf16) ||
+      make_kmajor_map(&p.tma_w, w, p.N, p.K, p.K, C::BNH, bf16))
+    return FRATTN_E_TMAP;
+  p.n_tiles_n = (p.N + C::BN - 1) / C::BN;
+  p.n_tiles = ((p.T + 255) / 256) * p.n_tiles_n;
+  auto kern = qkv_rope_gemm_pair_kernel<D, TI, TC>;
+  static unsigned long long attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bitv = 1ull << (dev & 63);
+  if (!(attr_set & bitv)) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+      return FRATTN_E_CUDA;
+    attr_set |= bitv;
+  }
+  const int pairs = sm_count_for_current_device() / 2;
+  const int np = p.n_tiles < pairs ? p.n_tiles : pairs;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(2 * np);
+  lc.blockDim = dim3(kQkvThreads);
+  lc.dynamicSmemBytes = C::SMEM;
+  lc.stream = st;
+  lc.attrs = &attr;
+  lc.numAttrs = 1;
+  if (cudaLaunchKernelEx(&lc, kern, p) != cudaSuccess) return FRATTN_E_CUDA;
+  return cudaGetLastError() == cudaSuccess ? 0 : FRATTN_E_CUDA;
+}
+
 template <int D, typename TI, typename TC>
 static int launch_qkv(QkvParams& p, const void* x, long long ldx, const void* w, bool bf16,
                       cudaStream_t st) {
+  if (qkv_use_pairs()) return launch_qkv_pair<D, TI, TC>(p, x, ldx, w, bf16, st);
   using C = QkvCfg<D>;
   if (make_kmajor_map(&p.tma_x, x, p.T, p.K, ldx, C::BM, bf16) ||
       make_kmajor_map(&p.tma_w, w, p.N, p.K, p.K, C::BN, bf16))
@@ -321,7 +529,7 @@ static int launch_qkv(QkvParams& p, const void* x, long long ldx, const void* w,
   }
   const int sms = sm_count_for_current_device();
   const int grid = p.n_tiles < sms ? p.n_tiles : sms;
-  kern<<<grid, 192, C::SMEM, st>>>(p);
+  kern<<<grid, kQkvThreads, C::SMEM, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? 0 : FRATTN_E_CUDA;
 }
 
@@ -385,4 +593,9 @@ extern "C" int frattn_qkv_rope(const void* x, long long x_stride, const void* w,
     case 128: return qkv_in<128>(p, x, x_stride, w, in_dtype, cs_dtype, st);
     default: return FRATTN_E_SHAPE;
   }
+}
+
+extern "C" int frattn_qkv_rope_set_pairs(int enable) {
+  frattn::g_qkv_pairs = enable ? 1 : 0;
+  return 0;
 }

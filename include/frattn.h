@@ -159,6 +159,11 @@ int frattn_fwd_pos(const void* q, const void* k, const void* v, const int32_t* p
 int frattn_qkv_rope(const void* x, long long x_stride, const void* w, const void* bias,
                     const void* cos, const void* sin, int cs_dtype, int T, int K, int H, int D,
                     int in_dtype, void* qkv, int32_t* status, void* stream);
+/* Kernel choice of frattn_qkv_rope (no counterpart in the reference): enable != 0
+ * (default) runs the GEMM on CTA pairs (tcgen05 cta_group::2, one M = 256 MMA over
+ * two SMs, each loading half of the weight tile), 0 on single CTAs (M = 128).
+ * Both give the same values (same accumulation order per output element). */
+int frattn_qkv_rope_set_pairs(int enable);
 int frattn_fwd_rotated(const void* q, const void* k, const void* v, long long q_stride,
                        long long k_stride, long long v_stride, const int32_t* cu_seqlens, int nseg,
                        int T, int H, int D, int max_seqlen, int in_dtype, void* out,

@@ -173,3 +173,23 @@ def test_projection_then_rotated_attention_matches_unfused(windowed):
     yq = torch.from_numpy(y).to(torch.bfloat16).to(DEV)
     o2 = fused_rope_attention(yq[:, 0], yq[:, 1], yq[:, 2], cos.to(DEV), sin.to(DEV), cu.to(DEV), max_seqlen=hint)
     assert (out.float() - o2.float()).abs().max().item() <= 2e-2
+
+
+@pytest.mark.parametrize("T,K,H,D", [(9216, 1280, 16, 80), (300, 200, 3, 64), (513, 136, 2, 128), (257, 96, 5, 48)])
+def test_cta_pairs_equal_single_ctas(T, K, H, D):
+    """The CTA-pair kernel (M = 256 over two SMs) and the single-CTA kernel compute
+    every output element with the same K order: identical results, ragged T included."""
+    from fused_rope_attn_b200 import _lib
+    x, w, b, cos, sin = proj_inputs(T, K, H, D, torch.bfloat16, seed=4)
+    args = (x.to(DEV), w.to(DEV), b.to(DEV), cos.to(DEV), sin.to(DEV), H)
+    lib = _lib.load()
+    try:
+        lib.frattn_qkv_rope_set_pairs(0)
+        single = qkv_rope_projection(*args)
+        lib.frattn_qkv_rope_set_pairs(1)
+        pairs = qkv_rope_projection(*args)
+        torch.cuda.synchronize()
+    finally:
+        lib.frattn_qkv_rope_set_pairs(1)
+    assert last_status(DEV) == 0
+    assert torch.equal(single, pairs), (single.float() - pairs.float()).abs().max().item()
