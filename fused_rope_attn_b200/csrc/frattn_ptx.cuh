@@ -318,3 +318,19 @@ __device__ __forceinline__ void umma_commit_pair_mc(uint32_t bar, uint16_t cta_m
       : "memory");
 }
 }  // namespace frattn
+
+namespace frattn {
+// 2-D tiled store of a shared-memory box (TMA; rows / columns past the tensor
+// are not written), tracked by the issuing thread's bulk group.
+__device__ __forceinline__ void tma_store_2d(const void* desc, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(desc)),
+               "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Every committed bulk group of this thread has finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Every committed bulk group of this thread has completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+}  // namespace frattn

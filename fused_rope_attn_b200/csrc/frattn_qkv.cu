@@ -40,6 +40,7 @@ constexpr int kQkvThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 
 struct QkvParams {
   CUtensorMap tma_x, tma_w;
+  CUtensorMap tma_out;  // [T, N] output, box {D, 128} (one head of one tile)
   const void* bias;  // [N] or nullptr
   const void* cos;   // [T, D/2]
   const void* sin;
@@ -58,9 +59,11 @@ struct QkvCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int ST_FIT = (227 * 1024 - 2048) / STAGE;
+  static constexpr int STG_BYTES = BM * BN * 2;  // output staging of one tile
+  static constexpr int ST_FIT = (227 * 1024 - 2048 - STG_BYTES) / STAGE;
   static constexpr int ST = ST_FIT > 6 ? 6 : ST_FIT;
-  static constexpr int OFF_BAR = ST * STAGE;
+  static constexpr int OFF_STG = ST * STAGE;
+  static constexpr int OFF_BAR = OFF_STG + STG_BYTES;
   static constexpr int SMEM = OFF_BAR + 256 + 1024;  // barriers + 1024-B alignment slack
   static_assert(BN % 16 == 0 && BN <= 256, "UMMA N");
   static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "128-B swizzle atoms");
@@ -102,60 +105,105 @@ __device__ __forceinline__ void load8_in(const TI* src, float (&v)[8]) {
 
 }  // namespace
 
-// Epilogue of one tile for the thread of accumulator row `row`: whole heads of
-// the N tile [n0, n0 + HPT D) from TMEM columns acc.. (bias, rounding to the
-// input type, rotation of q / k heads, 16-byte stores).
+// Epilogue of one tile for the thread of accumulator row `row` (row r of the
+// CTA's 128): whole heads of the N tile [n0, n0 + HPT D) from TMEM columns acc..
+// (bias, rounding to the input type, rotation of q / k heads) into the
+// shared-memory staging boxes [HPT][128][D] that TMA stores then write out
+// (rows of 32 threads land in one box: coalesced, full-sector writes, where
+// per-thread row stores wrote 32 separate half sectors per instruction).
+// cos / sin of the token of accumulator row `row`, loaded into registers before
+// the tile's accumulator is ready (their latency then hides behind the main
+// loop). Head dims above 80 load them per head instead (register budget).
+template <int D>
+struct QkvRowCs {
+  static constexpr bool kPrefetch = D <= 80;
+  float c[kPrefetch ? D / 2 : 1], s[kPrefetch ? D / 2 : 1];
+};
+
+template <int D, typename TC>
+__device__ __forceinline__ void qkv_row_cs(const QkvParams& p, int row, int n0, QkvRowCs<D>& cs) {
+  if constexpr (QkvRowCs<D>::kPrefetch) {
+    if (row >= p.T || n0 >= 2 * p.H * D) return;  // no q / k head in this tile
+    const TC* cr = static_cast<const TC*>(p.cos) + static_cast<size_t>(row) * (D / 2);
+    const TC* sr = static_cast<const TC*>(p.sin) + static_cast<size_t>(row) * (D / 2);
+#pragma unroll
+    for (int c = 0; c < D / 16; ++c) {
+      float a[8], b[8];
+      load8<TC>(cr + 8 * c, a);
+      load8<TC>(sr + 8 * c, b);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        cs.c[8 * c + e] = a[e];
+        cs.s[8 * c + e] = b[e];
+      }
+    }
+  }
+}
+
+// The tile's accumulator columns are released (lane 0 arrives on empty_bar, a
+// shared::cluster address) as soon as the last head has been read from TMEM.
 template <int D, int HPT, typename TI, typename TC>
-__device__ __forceinline__ void qkv_tile_epilogue(const QkvParams& p, uint32_t acc, int row, int n0) {
+__device__ __forceinline__ void qkv_tile_epilogue(const QkvParams& p, uint32_t acc, int row, int n0, uint8_t* stg,
+                                                  int r, const QkvRowCs<D>& cs, uint32_t empty_bar) {
   const TI* bias = static_cast<const TI*>(p.bias);
-  TI* out = static_cast<TI*>(p.out);
 #pragma unroll 1
   for (int hh = 0; hh < HPT; ++hh) {
     const int n = n0 + hh * D;
     if (n >= p.N) break;
-    uint32_t v[D];
+    uint32_t v[D];  // accumulator, then the finished values (fp32 bit patterns)
 #pragma unroll
     for (int c = 0; c < D / 16; ++c) {
       uint32_t (&chunk)[16] = *reinterpret_cast<uint32_t(*)[16]>(&v[16 * c]);
       tmem_ld16(acc + hh * D + 16 * c, chunk);
     }
     tmem_ld_wait();
+    if (hh == HPT - 1 || n + D >= p.N) {  // last head of the tile: TMEM no longer read
+      tc_fence_before();
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) mbar_arrive_cluster(empty_bar);
+    }
     if (row >= p.T) continue;
-    float x[D];
 #pragma unroll
     for (int c = 0; c < D / 8; ++c) {
       float b[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       if (bias) load8_in<TI>(bias + n + 8 * c, b);
 #pragma unroll
       for (int e = 0; e < 8; ++e)  // the value a plain projection stores
-        x[8 * c + e] = to_f32<TI>(from_f32<TI>(__uint_as_float(v[8 * c + e]) + b[e]));
+        v[8 * c + e] = __float_as_uint(to_f32<TI>(from_f32<TI>(__uint_as_float(v[8 * c + e]) + b[e])));
     }
     const int part = (n / D) / p.H;  // 0 q, 1 k, 2 v
     if (part < 2) {
-      const TC* cr = static_cast<const TC*>(p.cos) + static_cast<size_t>(row) * (D / 2);
-      const TC* sr = static_cast<const TC*>(p.sin) + static_cast<size_t>(row) * (D / 2);
 #pragma unroll
       for (int c = 0; c < D / 16; ++c) {
-        float cs[8], sn[8];
-        load8<TC>(cr + 8 * c, cs);
-        load8<TC>(sr + 8 * c, sn);
+        float c8[8], s8[8];
+        if constexpr (QkvRowCs<D>::kPrefetch) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            c8[e] = cs.c[8 * c + e];
+            s8[e] = cs.s[8 * c + e];
+          }
+        } else {
+          load8<TC>(static_cast<const TC*>(p.cos) + static_cast<size_t>(row) * (D / 2) + 8 * c, c8);
+          load8<TC>(static_cast<const TC*>(p.sin) + static_cast<size_t>(row) * (D / 2) + 8 * c, s8);
+        }
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const float x0 = x[8 * c + e], x1 = x[8 * c + e + D / 2];
-          x[8 * c + e] = x0 * cs[e] - x1 * sn[e];
-          x[8 * c + e + D / 2] = x0 * sn[e] + x1 * cs[e];
+          const float x0 = __uint_as_float(v[8 * c + e]), x1 = __uint_as_float(v[8 * c + e + D / 2]);
+          v[8 * c + e] = __float_as_uint(x0 * c8[e] - x1 * s8[e]);
+          v[8 * c + e + D / 2] = __float_as_uint(x0 * s8[e] + x1 * c8[e]);
         }
       }
     }
-    TI* dst = out + static_cast<size_t>(row) * p.N + n;
+    // row r of head hh's [128][D] staging box (written to global by a TMA store)
+    uint4* dst = reinterpret_cast<uint4*>(stg + (static_cast<size_t>(hh) * 128 + r) * D * 2);
 #pragma unroll
     for (int c = 0; c < D / 8; ++c) {
       uint4 w;
-      w.x = pack2<TI>(x[8 * c + 0], x[8 * c + 1]);
-      w.y = pack2<TI>(x[8 * c + 2], x[8 * c + 3]);
-      w.z = pack2<TI>(x[8 * c + 4], x[8 * c + 5]);
-      w.w = pack2<TI>(x[8 * c + 6], x[8 * c + 7]);
-      *reinterpret_cast<uint4*>(dst + 8 * c) = w;
+      w.x = pack2<TI>(__uint_as_float(v[8 * c + 0]), __uint_as_float(v[8 * c + 1]));
+      w.y = pack2<TI>(__uint_as_float(v[8 * c + 2]), __uint_as_float(v[8 * c + 3]));
+      w.z = pack2<TI>(__uint_as_float(v[8 * c + 4]), __uint_as_float(v[8 * c + 5]));
+      w.w = pack2<TI>(__uint_as_float(v[8 * c + 6]), __uint_as_float(v[8 * c + 7]));
+      dst[c] = w;
     }
   }
 }
@@ -174,7 +222,8 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_rope_gemm_kernel(const __g
   // full[ST] empty[ST] acc_full[2] acc_empty[2] drain
   auto bar = [&](int i) { return smem_u32(bars + i); };
   const int FULL = 0, EMPTY = ST, ACC_FULL = 2 * ST, ACC_EMPTY = 2 * ST + 2, DRAIN = 2 * ST + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 5);
+  const int STG_FREE = 2 * ST + 5, STG_FULL = 2 * ST + 6;  // output staging reusable / written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 7);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -188,10 +237,13 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_rope_gemm_kernel(const __g
       mbar_init(bar(ACC_EMPTY + i), 4);
     }
     mbar_init(bar(DRAIN), 1);
+    mbar_init(bar(STG_FREE), 1);
+    mbar_init(bar(STG_FULL), 128);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&p.tma_x);
     tma_prefetch_desc(&p.tma_w);
+    tma_prefetch_desc(&p.tma_out);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), 512);
@@ -263,18 +315,41 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_rope_gemm_kernel(const __g
     const int ew = warp & 3;  // TMEM lane quarter this warp may access
     const int r = ew * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(ew * 32) << 16);
+    const bool store_leader = warp == 2 && lane == 0;  // issues the tile's TMA stores
     uint32_t lt = 0;
     for (int t = blockIdx.x; t < p.n_tiles; t += gridDim.x, ++lt) {
       const int buf = lt & 1;
+      const int m0p = (t / p.n_tiles_n) * C::BM, n0p = (t % p.n_tiles_n) * C::BN;
+      QkvRowCs<D> rcs;
+      qkv_row_cs<D, TC>(p, m0p + r, n0p, rcs);  // before the accumulator wait
       const bool ok = qkv_wait(bar(ACC_FULL + buf), (lt >> 1) & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x34);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       const int m0 = (t / p.n_tiles_n) * C::BM, n0 = (t % p.n_tiles_n) * C::BN;
-      qkv_tile_epilogue<D, C::HPT, TI, TC>(p, lane_base + buf * 256u, m0 + r, n0);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(ACC_EMPTY + buf));
+      // the staging boxes are free once the previous tile's TMA stores have read them
+      if (lt > 0) {
+        if (store_leader) {
+          bulk_wait_read_all();
+          mbar_arrive(bar(STG_FREE));
+        }
+        if (!__all_sync(0xffffffffu, qkv_wait(bar(STG_FREE), (lt - 1) & 1, p, abort_flag,
+                                              FRATTN_STATUS_WAIT_TIMEOUT | 0x3A)))
+          break;
+      }
+      qkv_tile_epilogue<D, C::HPT, TI, TC>(p, lane_base + buf * 256u, m0 + r, n0, smem + C::OFF_STG, r, rcs,
+                                           mapa_shared(bar(ACC_EMPTY + buf), cluster_ctarank()));
+      fence_proxy_async_smem();  // staging writes visible to the TMA stores
+      mbar_arrive(bar(STG_FULL));
+      if (store_leader) {
+        if (!qkv_wait(bar(STG_FULL), lt & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x3B)) break;
+#pragma unroll 1
+        for (int hh = 0; hh < C::HPT; ++hh)
+          if (n0 + hh * D < p.N)
+            tma_store_2d(&p.tma_out, smem_u32(smem + C::OFF_STG) + hh * 128 * D * 2, n0 + hh * D, m0);
+        bulk_commit_group();
+      }
     }
+    if (store_leader) bulk_wait_all();  // output written before the CTA ends
   }
   tc_fence_before();
   __syncthreads();
@@ -303,9 +378,11 @@ struct QkvPairCfg {
   static constexpr int A_BYTES = 128 * BK * 2;
   static constexpr int B_BYTES = BNH * BK * 2;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int ST_FIT = (227 * 1024 - 2048) / STAGE;
+  static constexpr int STG_BYTES = 128 * BN * 2;  // output staging of the CTA's 128 rows
+  static constexpr int ST_FIT = (227 * 1024 - 2048 - STG_BYTES) / STAGE;
   static constexpr int ST = ST_FIT > 6 ? 6 : ST_FIT;
-  static constexpr int OFF_BAR = ST * STAGE;
+  static constexpr int OFF_STG = ST * STAGE;
+  static constexpr int OFF_BAR = OFF_STG + STG_BYTES;
   static constexpr int SMEM = OFF_BAR + 256 + 1024;
   static_assert(BN % 16 == 0 && BN <= 256 && BNH % 8 == 0, "UMMA N / swizzle atoms");
   static_assert(B_BYTES % 1024 == 0, "128-B swizzle atoms");
@@ -324,7 +401,8 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_rope_gemm_pair_kernel(cons
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   auto bar = [&](int i) { return smem_u32(bars + i); };
   const int FULL = 0, EMPTY = ST, ACC_FULL = 2 * ST, ACC_EMPTY = 2 * ST + 2, DRAIN = 2 * ST + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 5);
+  const int STG_FREE = 2 * ST + 5, STG_FULL = 2 * ST + 6;  // output staging reusable / written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * ST + 7);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -341,10 +419,13 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_rope_gemm_pair_kernel(cons
       mbar_init(bar(ACC_EMPTY + i), 8);  // 4 epilogue warps of each CTA (used in the leader)
     }
     mbar_init(bar(DRAIN), 1);
+    mbar_init(bar(STG_FREE), 1);
+    mbar_init(bar(STG_FULL), 128);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&p.tma_x);
     tma_prefetch_desc(&p.tma_w);
+    tma_prefetch_desc(&p.tma_out);
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(tmem_slot), 512);
@@ -419,18 +500,41 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_rope_gemm_pair_kernel(cons
     const int r = ew * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(ew * 32) << 16);
     const uint32_t acc_empty0 = mapa_shared(bar(ACC_EMPTY), 0);
+    const bool store_leader = warp == 2 && lane == 0;  // issues the tile's TMA stores
     uint32_t lt = 0;
     for (int t = pair; t < p.n_tiles; t += npairs, ++lt) {
       const int buf = lt & 1;
+      const int m0p = (t / p.n_tiles_n) * 256 + 128 * static_cast<int>(rank), n0p = (t % p.n_tiles_n) * C::BN;
+      QkvRowCs<D> rcs;
+      qkv_row_cs<D, TC>(p, m0p + r, n0p, rcs);  // before the accumulator wait
       const bool ok = qkv_wait(bar(ACC_FULL + buf), (lt >> 1) & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x38);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       const int m0 = (t / p.n_tiles_n) * 256 + 128 * static_cast<int>(rank), n0 = (t % p.n_tiles_n) * C::BN;
-      qkv_tile_epilogue<D, C::HPT, TI, TC>(p, lane_base + buf * 256u, m0 + r, n0);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8u * buf);
+      // the staging boxes are free once the previous tile's TMA stores have read them
+      if (lt > 0) {
+        if (store_leader) {
+          bulk_wait_read_all();
+          mbar_arrive(bar(STG_FREE));
+        }
+        if (!__all_sync(0xffffffffu, qkv_wait(bar(STG_FREE), (lt - 1) & 1, p, abort_flag,
+                                              FRATTN_STATUS_WAIT_TIMEOUT | 0x3A)))
+          break;
+      }
+      qkv_tile_epilogue<D, C::HPT, TI, TC>(p, lane_base + buf * 256u, m0 + r, n0, smem + C::OFF_STG, r, rcs,
+                                           acc_empty0 + 8u * buf);
+      fence_proxy_async_smem();  // staging writes visible to the TMA stores
+      mbar_arrive(bar(STG_FULL));
+      if (store_leader) {
+        if (!qkv_wait(bar(STG_FULL), lt & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x3B)) break;
+#pragma unroll 1
+        for (int hh = 0; hh < C::HPT; ++hh)
+          if (n0 + hh * D < p.N)
+            tma_store_2d(&p.tma_out, smem_u32(smem + C::OFF_STG) + hh * 128 * D * 2, n0 + hh * D, m0);
+        bulk_commit_group();
+      }
     }
+    if (store_leader) bulk_wait_all();  // output written before the CTA ends
   }
   tc_fence_before();
   cluster_sync_all();  // no CTA leaves while its pair may still signal it
@@ -469,13 +573,40 @@ static int make_kmajor_map(CUtensorMap* m, const void* base, int rows, int K, lo
   return r == CUDA_SUCCESS ? 0 : FRATTN_E_TMAP;
 }
 
+// [T, N] output as a 2-D TMA map with box {D, 128} (one head of a 128-row tile),
+// no swizzle: the staging boxes are dense [128][D] rows.
+static int make_out_map(CUtensorMap* m, void* base, int T, int N, int D, bool bf16) {
+  typedef CUresult (*PFN)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                          const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                          CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                          CUtensorMapFloatOOBfill);
+  static PFN enc = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      enc = reinterpret_cast<PFN>(f);
+  });
+  if (!enc) return FRATTN_E_TMAP;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(T)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(N) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(D), 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : FRATTN_E_TMAP;
+}
+
 // CTA-pair launch (cluster of 2).
 template <int D, typename TI, typename TC>
 static int launch_qkv_pair(QkvParams& p, const void* x, long long ldx, const void* w, bool bf16,
                            cudaStream_t st) {
   using C = QkvPairCfg<D>;
   if (make_kmajor_map(&p.tma_x, x, p.T, p.K, ldx, 128, bf16) ||
-      make_kmajor_map(&p.tma_w, w, p.N, p.K, p.K, C::BNH, bf16))
+      make_kmajor_map(&p.tma_w, w, p.N, p.K, p.K, C::BNH, bf16) || make_out_map(&p.tma_out, p.out, p.T, p.N, D, bf16))
     return FRATTN_E_TMAP;
   p.n_tiles_n = (p.N + C::BN - 1) / C::BN;
   p.n_tiles = ((p.T + 255) / 256) * p.n_tiles_n;
@@ -513,7 +644,7 @@ static int launch_qkv(QkvParams& p, const void* x, long long ldx, const void* w,
   if (qkv_use_pairs()) return launch_qkv_pair<D, TI, TC>(p, x, ldx, w, bf16, st);
   using C = QkvCfg<D>;
   if (make_kmajor_map(&p.tma_x, x, p.T, p.K, ldx, C::BM, bf16) ||
-      make_kmajor_map(&p.tma_w, w, p.N, p.K, p.K, C::BN, bf16))
+      make_kmajor_map(&p.tma_w, w, p.N, p.K, p.K, C::BN, bf16) || make_out_map(&p.tma_out, p.out, p.T, p.N, D, bf16))
     return FRATTN_E_TMAP;
   p.n_tiles_n = (p.N + C::BN - 1) / C::BN;
   p.n_tiles = ((p.T + C::BM - 1) / C::BM) * p.n_tiles_n;
