@@ -36,7 +36,14 @@ unsigned long long frattn_wait_limit_ns();  // frattn.cu
 static int g_qkv_pairs = 1;
 static bool qkv_use_pairs() { return g_qkv_pairs != 0; }
 
-constexpr int kQkvThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+#ifndef FRATTN_QKV_EPI_WARPS
+#define FRATTN_QKV_EPI_WARPS 4
+#endif
+// Epilogue warps: 4 (one per TMEM lane quarter) or 8 (two per quarter, taking
+// alternate heads of a tile; 8 measured slower: register spills at 320 threads).
+constexpr int kEpiWarps = FRATTN_QKV_EPI_WARPS;
+constexpr int kHeadStep = kEpiWarps / 4;
+constexpr int kQkvThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, the rest epilogue
 
 struct QkvParams {
   CUtensorMap tma_x, tma_w;
@@ -144,10 +151,10 @@ __device__ __forceinline__ void qkv_row_cs(const QkvParams& p, int row, int n0, 
 // shared::cluster address) as soon as the last head has been read from TMEM.
 template <int D, int HPT, typename TI, typename TC>
 __device__ __forceinline__ void qkv_tile_epilogue(const QkvParams& p, uint32_t acc, int row, int n0, uint8_t* stg,
-                                                  int r, const QkvRowCs<D>& cs, uint32_t empty_bar) {
+                                                  int r, const QkvRowCs<D>& cs, uint32_t empty_bar, int h0) {
   const TI* bias = static_cast<const TI*>(p.bias);
 #pragma unroll 1
-  for (int hh = 0; hh < HPT; ++hh) {
+  for (int hh = h0; hh < HPT; hh += kHeadStep) {
     const int n = n0 + hh * D;
     if (n >= p.N) break;
     uint32_t v[D];  // accumulator, then the finished values (fp32 bit patterns)
@@ -157,7 +164,7 @@ __device__ __forceinline__ void qkv_tile_epilogue(const QkvParams& p, uint32_t a
       tmem_ld16(acc + hh * D + 16 * c, chunk);
     }
     tmem_ld_wait();
-    if (hh == HPT - 1 || n + D >= p.N) {  // last head of the tile: TMEM no longer read
+    if (hh + kHeadStep >= HPT || n + kHeadStep * D >= p.N) {  // this warp's last head: TMEM no longer read
       tc_fence_before();
       __syncwarp();
       if ((threadIdx.x & 31) == 0) mbar_arrive_cluster(empty_bar);
@@ -234,11 +241,11 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_rope_gemm_kernel(const __g
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(ACC_FULL + i), 1);
-      mbar_init(bar(ACC_EMPTY + i), 4);
+      mbar_init(bar(ACC_EMPTY + i), kEpiWarps);
     }
     mbar_init(bar(DRAIN), 1);
     mbar_init(bar(STG_FREE), 1);
-    mbar_init(bar(STG_FULL), 128);
+    mbar_init(bar(STG_FULL), 32 * kEpiWarps);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&p.tma_x);
@@ -337,7 +344,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_rope_gemm_kernel(const __g
           break;
       }
       qkv_tile_epilogue<D, C::HPT, TI, TC>(p, lane_base + buf * 256u, m0 + r, n0, smem + C::OFF_STG, r, rcs,
-                                           mapa_shared(bar(ACC_EMPTY + buf), cluster_ctarank()));
+                                           mapa_shared(bar(ACC_EMPTY + buf), cluster_ctarank()), (warp - 2) >> 2);
       fence_proxy_async_smem();  // staging writes visible to the TMA stores
       mbar_arrive(bar(STG_FULL));
       if (store_leader) {
@@ -416,11 +423,11 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_rope_gemm_pair_kernel(cons
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar(ACC_FULL + i), 1);
-      mbar_init(bar(ACC_EMPTY + i), 8);  // 4 epilogue warps of each CTA (used in the leader)
+      mbar_init(bar(ACC_EMPTY + i), 2 * kEpiWarps);  // epilogue warps of both CTAs (used in the leader)
     }
     mbar_init(bar(DRAIN), 1);
     mbar_init(bar(STG_FREE), 1);
-    mbar_init(bar(STG_FULL), 128);
+    mbar_init(bar(STG_FULL), 32 * kEpiWarps);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&p.tma_x);
@@ -522,7 +529,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_rope_gemm_pair_kernel(cons
           break;
       }
       qkv_tile_epilogue<D, C::HPT, TI, TC>(p, lane_base + buf * 256u, m0 + r, n0, smem + C::OFF_STG, r, rcs,
-                                           acc_empty0 + 8u * buf);
+                                           acc_empty0 + 8u * buf, (warp - 2) >> 2);
       fence_proxy_async_smem();  // staging writes visible to the TMA stores
       mbar_arrive(bar(STG_FULL));
       if (store_leader) {
