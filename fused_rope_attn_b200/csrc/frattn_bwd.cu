@@ -23,13 +23,14 @@
 //                   dQ_tile = dS K                      (SS: dS^T written to smem
 //                                                        as an MN-major A operand)
 //                 The 256 compute threads (one key row and half of the columns
-//                 each) turn S^T, dP^T into P^T and dS^T; the dQ tile (q rows =
-//                 TMEM lanes) is added to the fp32 [H, T, D] accumulator with
-//                 vector atomics, one row per lane. dK is scaled and inverse-
+//                 each) turn S^T, dP^T into P^T and dS^T; 128 dQ threads add the
+//                 dQ tile (q rows = TMEM lanes) to the fp32 [H, T, D] accumulator
+//                 with vector atomics, one row per lane. dK is scaled and inverse-
 //                 rotated in the epilogue; dV is stored as is.
 //   bwd_dq        one thread per (token, head): dq = R^T(dq_acc / sqrt(D))
-// Warp roles of bwd_main (320 threads): warp 0 TMA producer (K, V once; Q, dO
-// per q tile, two stages), warp 1 TMEM owner + MMA issuer, warps 2-9 compute.
+// Warp roles of bwd_main (448 threads): warp 0 TMA producer (K, V once; Q, dO
+// per q tile, two stages), warp 1 TMEM owner + MMA issuer, warps 2-9 compute,
+// warps 10-13 dQ (TMEM read and atomics, overlapping the next tile's compute).
 // Every mbarrier wait is bounded (status code, unwind, TMEM freed).
 #include "frattn_kernel.cuh"
 
@@ -213,7 +214,9 @@ static __device__ unsigned long long g_bwd_trace[16 * 32];
 #else
 #define BT(ev, i) do { } while (0)
 #endif
-constexpr int kBwdThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 compute
+// warp 0 TMA, warp 1 MMA, warps 2-9 compute, warps 10-13 dQ (144 registers per
+// thread at one CTA per SM)
+constexpr int kBwdThreads = 448;
 template <int D, typename TI, typename TC>
 __global__ void __launch_bounds__(kBwdThreads, 1) bwd_main(const __grid_constant__ BwdParams p) {
   using C = BwdCfg<D>;
@@ -254,7 +257,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_main(const __grid_constant
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NBAR; ++i)
-      mbar_init(bar(i), (i == DS_READY || i == DQ_FREE || i >= VEC_READY) ? 256 : 1);
+      mbar_init(bar(i), (i == DS_READY || i >= VEC_READY) ? 256 : i == DQ_FREE ? 128 : 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -354,7 +357,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_main(const __grid_constant
       umma_commit(bar(DRAIN));
       bwd_drain(bar(DRAIN), 0, p.wait_limit_ns);
     }
-  } else {
+  } else if (warp < 10) {
     // -------------------------------------------------------------- compute
     // 8 warps: warp w reads TMEM lane quarter w & 3 (rows t); the two warps of
     // a quarter split the work by column halves (hf = 0, 1).
@@ -371,8 +374,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_main(const __grid_constant
       }
     }
     const float sl2 = 1.4426950408889634f * rsqrtf(static_cast<float>(D));
-    constexpr int DQH = D / 2;  // dQ columns per warp
-    float* dq_head = p.dq_acc + static_cast<size_t>(h) * p.T * D;                     // [T, D] of head h
     // this thread's lse (half 0) or delta (half 1) value of row t of a q tile,
     // loaded one tile ahead
     auto row_term = [&](int q0) -> float {
@@ -447,96 +448,109 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_main(const __grid_constant
       mbar_arrive(bar(DS_READY));
       if (t == 0 && hf == 0) BT(6, i);
       if (i + 1 < nq) term = row_term(q_tile(i + 1));  // latency hidden by the dQ phase
-      // dQ tile (TMEM lane = q row): this warp's 32 rows x D/2 columns are added
-      // to the fp32 [T, D] accumulator rows of head h with vector atomics
-      ok = bwd_wait_warp(bar(DQ_FULL), i & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x68);
-      if (t == 0 && hf == 0) BT(7, i);
-      if (!ok) break;
-      tc_fence_after();
-      {
-        uint32_t dq[DQH];
-        if constexpr (DQH % 16 == 0) {
-#pragma unroll
-          for (int c = 0; c < DQH / 16; ++c)
-            tmem_ld16(lane_addr + C::T_DQ + hf * DQH + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(&dq[16 * c]));
-        } else {
-#pragma unroll
-          for (int c = 0; c < DQH / 8; ++c)
-            tmem_ld8(lane_addr + C::T_DQ + hf * DQH + 8 * c, *reinterpret_cast<uint32_t(*)[8]>(&dq[8 * c]));
-        }
-        tmem_ld_wait();
-        tc_fence_before();
-        mbar_arrive(bar(DQ_FREE));  // the S columns may take the next S^T
-        if (t == 0 && hf == 0) BT(8, i);
-        // One row per lane: the 32 lanes of an atomic instruction hit 32
-        // different cache lines (same-line vector atomics serialise in L2; a
-        // staged bulk reduce-add of the contiguous tile measured slower, its
-        // shared-memory reads drain at a few bytes per clock).
-        const int q = q0 + t;
-        if (q < qb) {
-          float4* dst = reinterpret_cast<float4*>(dq_head + static_cast<size_t>(q) * D + hf * DQH);
-#pragma unroll
-          for (int c = 0; c < DQH / 4; ++c)
-            atomicAdd(dst + c, make_float4(__uint_as_float(dq[4 * c]), __uint_as_float(dq[4 * c + 1]),
-                                           __uint_as_float(dq[4 * c + 2]), __uint_as_float(dq[4 * c + 3])));
-        }
-        if (t == 0 && hf == 0) BT(9, i);
-      }
     }
     // epilogue: half 0 stores dV as is, half 1 stores dK scaled and rotated back;
     // keys outside every segment get 0
     if (ok && nq > 0) ok = bwd_wait_warp(bar(ACC_FULL), 0, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x69);
     tc_fence_after();
-    uint32_t acc[D];
-    if (ok && nq > 0) {
-#pragma unroll
-      for (int c = 0; c < D / 16; ++c)
-        tmem_ld16(lane_addr + (hf ? C::T_DK : C::T_DV) + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(&acc[16 * c]));
-      tmem_ld_wait();
-    }
-    if (key < kc1 && (ok || nq == 0)) {
-      const bool has = nq > 0 && klo < khi;
-      const size_t base = (static_cast<size_t>(key) * p.H + h) * D;
-      if (hf == 0) {
-        TI* dvp = static_cast<TI*>(p.dv) + base;
-#pragma unroll
-        for (int c = 0; c < D / 8; ++c) {
-          uint4 w;
-          uint32_t* ww = reinterpret_cast<uint32_t*>(&w);
-#pragma unroll
-          for (int e = 0; e < 8; e += 2)
-            ww[e / 2] = pack2<TI>(has ? __uint_as_float(acc[8 * c + e]) : 0.f,
-                                  has ? __uint_as_float(acc[8 * c + e + 1]) : 0.f);
-          *reinterpret_cast<uint4*>(dvp + 8 * c) = w;
+    // (8-column TMEM chunks: a few registers at a time; loads are warp-wide,
+    // stores only for rows that are keys of this chunk)
+    const bool loaded = ok && nq > 0;
+    const bool store = key < kc1 && (ok || nq == 0);
+    const bool has = nq > 0 && klo < khi;
+    const size_t base = (static_cast<size_t>(key) * p.H + h) * D;
+    if (hf == 0) {
+      TI* dvp = static_cast<TI*>(p.dv) + base;
+#pragma unroll 1
+      for (int c = 0; c < D / 8; ++c) {
+        uint32_t a8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (loaded) {
+          tmem_ld8(lane_addr + C::T_DV + 8 * c, a8);
+          tmem_ld_wait();
         }
-      } else {
-        TI* dkp = static_cast<TI*>(p.dk) + base;
-        const float scale = rsqrtf(static_cast<float>(D));
-        const TC* cr = static_cast<const TC*>(p.cos) + static_cast<size_t>(key) * (D / 2);
-        const TC* sr = static_cast<const TC*>(p.sin) + static_cast<size_t>(key) * (D / 2);
+        uint4 w;
+        uint32_t* ww = reinterpret_cast<uint32_t*>(&w);
 #pragma unroll
-        for (int c = 0; c < D / 16; ++c) {
-          float cs[8], sn[8];
-          load8<TC>(cr + 8 * c, cs);
-          load8<TC>(sr + 8 * c, sn);
-          uint4 oa, ob;
-          uint32_t* wa = reinterpret_cast<uint32_t*>(&oa);
-          uint32_t* wb = reinterpret_cast<uint32_t*>(&ob);
+        for (int e = 0; e < 8; e += 2)
+          ww[e / 2] = pack2<TI>(has ? __uint_as_float(a8[e]) : 0.f, has ? __uint_as_float(a8[e + 1]) : 0.f);
+        if (store) *reinterpret_cast<uint4*>(dvp + 8 * c) = w;
+      }
+    } else {
+      TI* dkp = static_cast<TI*>(p.dk) + base;
+      const float scale = rsqrtf(static_cast<float>(D));
+      const int krow = store ? key : 0;
+      const TC* cr = static_cast<const TC*>(p.cos) + static_cast<size_t>(krow) * (D / 2);
+      const TC* sr = static_cast<const TC*>(p.sin) + static_cast<size_t>(krow) * (D / 2);
+#pragma unroll 1
+      for (int c = 0; c < D / 16; ++c) {
+        uint32_t y0r[8] = {0, 0, 0, 0, 0, 0, 0, 0}, y1r[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (loaded) {
+          tmem_ld8(lane_addr + C::T_DK + 8 * c, y0r);
+          tmem_ld8(lane_addr + C::T_DK + D / 2 + 8 * c, y1r);
+          tmem_ld_wait();
+        }
+        float cs[8], sn[8];
+        load8<TC>(cr + 8 * c, cs);
+        load8<TC>(sr + 8 * c, sn);
+        uint4 oa, ob;
+        uint32_t* wa = reinterpret_cast<uint32_t*>(&oa);
+        uint32_t* wb = reinterpret_cast<uint32_t*>(&ob);
 #pragma unroll
-          for (int e = 0; e < 8; e += 2) {
-            float a[2], bb[2];
+        for (int e = 0; e < 8; e += 2) {
+          float a[2], bb[2];
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const float y0 = has ? __uint_as_float(acc[8 * c + e + u]) * scale : 0.f;
-              const float y1 = has ? __uint_as_float(acc[D / 2 + 8 * c + e + u]) * scale : 0.f;
-              a[u] = y0 * cs[e + u] + y1 * sn[e + u];
-              bb[u] = y1 * cs[e + u] - y0 * sn[e + u];
-            }
-            wa[e / 2] = pack2<TI>(a[0], a[1]);
-            wb[e / 2] = pack2<TI>(bb[0], bb[1]);
+          for (int u = 0; u < 2; ++u) {
+            const float y0 = has ? __uint_as_float(y0r[e + u]) * scale : 0.f;
+            const float y1 = has ? __uint_as_float(y1r[e + u]) * scale : 0.f;
+            a[u] = y0 * cs[e + u] + y1 * sn[e + u];
+            bb[u] = y1 * cs[e + u] - y0 * sn[e + u];
           }
+          wa[e / 2] = pack2<TI>(a[0], a[1]);
+          wb[e / 2] = pack2<TI>(bb[0], bb[1]);
+        }
+        if (store) {
           *reinterpret_cast<uint4*>(dkp + 8 * c) = oa;
           *reinterpret_cast<uint4*>(dkp + D / 2 + 8 * c) = ob;
+        }
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- dQ warps
+    // Read each q tile's dQ (TMEM lane = q row), free the columns for the next
+    // S^T, and add the row to the fp32 [H, T, D] accumulator with vector atomics
+    // (one row per lane: 32 different cache lines per instruction; same-line
+    // vector atomics serialise in L2, and a staged bulk reduce-add drained its
+    // shared memory at a few bytes per clock). The compute warps meanwhile go on
+    // with the next tile.
+    const int t = ((warp & 3) << 5) | lane;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    float* dq_head = p.dq_acc + static_cast<size_t>(h) * p.T * D;  // [T, D] of head h
+    for (int i = 0; i < nq; ++i) {
+      if (!bwd_wait_warp(bar(DQ_FULL), i & 1, p, abort_flag, FRATTN_STATUS_WAIT_TIMEOUT | 0x68)) break;
+      tc_fence_after();
+      // head dims up to 80 in one pass (registers); larger ones in two halves,
+      // the columns freed after the second
+      constexpr int NP = D <= 80 ? 1 : 2, W = D / NP;
+      const int q = q_tile(i) + t;
+      float4* dst = reinterpret_cast<float4*>(dq_head + static_cast<size_t>(q < qb ? q : 0) * D);
+#pragma unroll 1
+      for (int part = 0; part < NP; ++part) {
+        uint32_t dq[W];
+        static_assert(W % 8 == 0, "8-column TMEM chunks");
+#pragma unroll
+        for (int c = 0; c < W / 8; ++c)
+          tmem_ld8(lane_addr + C::T_DQ + part * W + 8 * c, *reinterpret_cast<uint32_t(*)[8]>(&dq[8 * c]));
+        tmem_ld_wait();
+        if (part == NP - 1) {
+          tc_fence_before();
+          mbar_arrive(bar(DQ_FREE));  // the S columns may take the next S^T
+        }
+        if (q < qb) {
+#pragma unroll
+          for (int c = 0; c < W / 4; ++c)
+            atomicAdd(dst + part * (W / 4) + c,
+                      make_float4(__uint_as_float(dq[4 * c]), __uint_as_float(dq[4 * c + 1]),
+                                  __uint_as_float(dq[4 * c + 2]), __uint_as_float(dq[4 * c + 3])));
         }
       }
     }
