@@ -7,11 +7,12 @@ attention, output projection, SiLU-gated MLP 1280 -> 3420 -> 1280), hidden
 windows elsewhere, random weights ~N(0, 0.02). The reference ships no encoder;
 this is harness code, not part of the kernel contract.
 
-Token flow (Qwen2.5-VL): patch embeddings are window-shuffled once
-(``window_shuffle``), every layer runs in window order (windowed layers use the
+Token flow (Qwen2.5-VL): patch embeddings are window-shuffled once (one
+gather kernel), every layer runs in window order (windowed layers use the
 window ``cu_seqlens``, full layers one segment per image/clip), and the output
-is unshuffled at the end. cos/sin come from ``compute_rope_2d`` with the same
-window permutation.
+is unshuffled at the end. The permutation, the window ``cu_seqlens`` and the
+window-ordered cos/sin come from the device window plan (``frattn_window_plan``,
+equal to ``get_window_index`` / ``compute_rope_2d`` of the reference).
 
 Attention implementations (``attn=``):
 * ``"fused"``    — ``fused_rope_attention`` (this repository's sm_100a kernel);
@@ -35,6 +36,7 @@ import torch
 from .fused_attn import (compute_rope_2d, fused_attention_rotated, fused_rope_attention, fused_rope_attention_fp8,
                          qkv_rope_projection)
 from .utils import get_window_index, segments_per_image, window_shuffle, window_unshuffle
+from .window_plan import window_plan_device, window_shuffle_device, window_unshuffle_device
 
 __all__ = ["EncoderConfig", "VisionEncoder", "encoder_inputs", "rope_unfused", "attention_fp32"]
 
@@ -163,17 +165,26 @@ class VisionEncoder(torch.nn.Module):
         return torch.nn.functional.rms_norm(x, (x.shape[-1],), weight, self.cfg.eps)
 
     def plan(self, grid_thw):
-        """Window permutation, cu_seqlens of both layer kinds and window-ordered cos/sin."""
+        """Window permutation, cu_seqlens of both layer kinds and window-ordered cos/sin,
+        built on the device (``frattn_window_plan``: no host index arithmetic, no
+        host sync). The longest segments come from the grid: a window holds at
+        most (window_size / patch_size)^2 tokens, an image / clip t h w."""
         c = self.cfg
-        widx, cu_win = get_window_index(grid_thw, window_size=c.window_size, spatial_merge_size=c.merge,
-                                        patch_size=c.patch_size)
-        cu_full = segments_per_image(grid_thw)
-        cos, sin = compute_rope_2d(grid_thw, c.head_dim, c.merge, c.theta, self.device, torch.float32,
-                                   window_idx=widx)
-        lw = (cu_win[1:] - cu_win[:-1]).max().item()
-        lf = (cu_full[1:] - cu_full[:-1]).max().item()
-        return dict(widx=widx.to(self.device), cu_win=cu_win.to(self.device), cu_full=cu_full.to(self.device),
-                    max_win=int(lw), max_full=int(lf), cos=cos, sin=sin)
+        cu_full = segments_per_image(grid_thw, device=self.device)
+        lw = min((c.window_size // c.patch_size) ** 2, max(int(h) * int(w) for _, h, w in grid_thw))
+        lf = max(int(t) * int(h) * int(w) for t, h, w in grid_thw)
+        if self.device.type != "cuda":  # the fp32 harness on CPU (multi-process tests): host plan
+            widx, cu_win = get_window_index(grid_thw, window_size=c.window_size, spatial_merge_size=c.merge,
+                                            patch_size=c.patch_size)
+            cos, sin = compute_rope_2d(grid_thw, c.head_dim, c.merge, c.theta, self.device, torch.float32,
+                                       window_idx=widx)
+            return dict(widx=widx, cu_win=cu_win, cu_full=cu_full, max_win=int(lw), max_full=int(lf), cos=cos,
+                        sin=sin)
+        dp = window_plan_device(grid_thw, window_size=c.window_size, spatial_merge_size=c.merge,
+                                patch_size=c.patch_size, device=self.device, head_dim=c.head_dim, theta=c.theta,
+                                positions=False)
+        return dict(widx=dp["window_index"], cu_win=dp["cu_seqlens"], cu_full=cu_full, max_win=int(lw),
+                    max_full=int(lf), cos=dp["cos"], sin=dp["sin"])
 
     def forward(self, x: torch.Tensor, grid_thw, attn: str = "fused", plan=None, layer_hook=None,
                 attn_hook=None):
@@ -184,7 +195,9 @@ class VisionEncoder(torch.nn.Module):
         c = self.cfg
         plan = plan or self.plan(grid_thw)
         T = x.shape[0]
-        h = window_shuffle(x, plan["widx"], spatial_merge_size=c.merge)
+        on_gpu = x.device.type == "cuda"
+        shuffle = window_shuffle_device if on_gpu else window_shuffle
+        h = shuffle(x, plan["widx"], spatial_merge_size=c.merge)
         for i, L in enumerate(self.layers):
             full = i in c.full_layers
             cu = plan["cu_full"] if full else plan["cu_win"]
@@ -216,7 +229,8 @@ class VisionEncoder(torch.nn.Module):
             h = h + torch.nn.functional.linear(a, L["down_w"])
             if layer_hook is not None:
                 layer_hook(i, h)
-        return window_unshuffle(h, plan["widx"], spatial_merge_size=c.merge)
+        unshuffle = window_unshuffle_device if on_gpu else window_unshuffle
+        return unshuffle(h, plan["widx"], spatial_merge_size=c.merge)
 
 
 def encoder_inputs(grid_thw, hidden=1280, seed=0, device="cuda", dtype=torch.bfloat16):
