@@ -565,19 +565,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) bwd_main(const __grid_constant
 
 // ------------------------------------------------------------------ host
 static int make_rows_map(CUtensorMap* m, const void* base, int T, int H, int D, bool bf16) {
-  typedef CUresult (*PFN)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                          const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
-                          CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
-                          CUtensorMapFloatOOBfill);
-  static PFN enc = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      enc = reinterpret_cast<PFN>(f);
-  });
+  const TmapEncodeFn enc = tmap_encoder();
   if (!enc) return FRATTN_E_TMAP;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(T)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(H) * D * 2};

@@ -1403,6 +1403,24 @@ __global__ void __launch_bounds__(kPrepThreads, 1)
 }
 
 // ------------------------------------------------------------------ launch
+// cuTensorMapEncodeTiled from the driver (looked up once per process; nullptr
+// when the driver does not provide it).
+typedef CUresult (*TmapEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+inline TmapEncodeFn tmap_encoder() {
+  static TmapEncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<TmapEncodeFn>(f);
+  });
+  return fn;
+}
+
 inline int sm_count_for_current_device() {
   static int cache[64] = {0};
   int dev = 0;

@@ -555,19 +555,7 @@ __global__ void __launch_bounds__(kQkvThreads, 1) qkv_rope_gemm_pair_kernel(cons
 // box {64, box_rows} and 128-byte swizzle.
 static int make_kmajor_map(CUtensorMap* m, const void* base, int rows, int K, long long ld,
                            int box_rows, bool bf16) {
-  typedef CUresult (*PFN)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                          const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
-                          CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
-                          CUtensorMapFloatOOBfill);
-  static PFN enc = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      enc = reinterpret_cast<PFN>(f);
-  });
+  const TmapEncodeFn enc = tmap_encoder();
   if (!enc) return FRATTN_E_TMAP;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
@@ -583,19 +571,7 @@ static int make_kmajor_map(CUtensorMap* m, const void* base, int rows, int K, lo
 // [T, N] output as a 2-D TMA map with box {D, 128} (one head of a 128-row tile),
 // no swizzle: the staging boxes are dense [128][D] rows.
 static int make_out_map(CUtensorMap* m, void* base, int T, int N, int D, bool bf16) {
-  typedef CUresult (*PFN)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                          const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
-                          CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
-                          CUtensorMapFloatOOBfill);
-  static PFN enc = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      enc = reinterpret_cast<PFN>(f);
-  });
+  const TmapEncodeFn enc = tmap_encoder();
   if (!enc) return FRATTN_E_TMAP;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(T)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(N) * 2};
